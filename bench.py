@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the C3 B200 hot path: fused Linear+bias+ReLU forward + captured backward.
+
+Workload (with its forward): one training step of the region
+Y = relu(X W^T + b) at global batch M=16384, N=K=4096, bf16 operands, fp32 accumulation:
+  forward  Y, mask = c3cu_linear_bias_relu_fwd(X, W, b)
+  backward dZ, db  = c3cu_relu_mask_db(dY, mask); dW = dZ^T X; dX = dZ W
+  N > 1    rows of X / dY are sharded across ranks (strong scaling at fixed global batch);
+           the packed [dW | db] fp32 buffer is summed by an NCCL all-reduce on a separate
+           stream, overlapped with the dX GEMM.
+Metric: whole-job TFLOP/s = 3 * 2 * M * N * K / step time (max over ranks, CUDA events).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl c3|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M_GLOBAL, N_DIM, K_DIM = 16384, 4096, 4096
+METRIC = "Fused Linear+ReLU fwd+bwd TFLOP/s (% of tensor peak) at 1/2/4/8 B200"
+UNIT = "TFLOP/s"
+WORKLOAD = "linear_bias_relu_train_step_cfg3"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), \
+            d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML during the timed region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: the line carries no clock record
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.05)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def record(self):
+        if self._nv is None or not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference's CPU arithmetic (C restatement, all host threads) on a bounded sample
+    of the same step: forward rows, ReLU-backward + db rows, dX rows and dW rows."""
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    import oracle
+    threads = oracle.default_threads()
+    rng = np.random.default_rng(0)
+    bf = lambda a: a.astype(np.float32)  # values are drawn on the bf16 grid below
+    def bf16_grid(a):
+        u = a.astype(np.float32).view(np.uint32)
+        return ((u + 0x7fff + ((u >> 16) & 1)) & 0xffff0000).view(np.float32)
+    W = bf16_grid(rng.standard_normal((N_DIM, K_DIM), dtype=np.float32) * 0.02)
+    b = rng.standard_normal(N_DIM, dtype=np.float32) * 0.01
+    rows = max(threads, 8)          # sampled rows of X / dY per step
+    wrows = max(1, threads // 4)    # sampled rows of dW (each spans all M rows)
+    Mw = M_GLOBAL // 4              # dW rows reduce over a quarter of the batch per step
+    X = bf16_grid(rng.standard_normal((rows, K_DIM), dtype=np.float32))
+    dY = bf16_grid(rng.standard_normal((rows, N_DIM), dtype=np.float32) * 1e-3)
+    Xw = bf16_grid(rng.standard_normal((Mw, K_DIM), dtype=np.float32))
+    dZw = bf16_grid(rng.standard_normal((Mw, wrows), dtype=np.float32) * 1e-3)
+
+    def step():
+        out, z = oracle.region_fwd(X, W, b, transB=True, threads=threads)
+        dZ = oracle.relu_bwd(dY, z)
+        oracle.sum_reduce(dZ, 0)
+        oracle.matmul(dZ, W, threads=threads)
+        oracle.matmul(dZw, Xw, transA=True, threads=threads)
+        return 2.0 * rows * N_DIM * K_DIM * 2 + 2.0 * wrows * K_DIM * Mw
+
+    for _ in range(args.warmup):
+        step()
+    flops, t0 = 0.0, time.perf_counter()
+    for _ in range(args.steps):
+        flops += step()
+    dt = time.perf_counter() - t0
+    value = flops / dt / 1e12
+    sample = (f"per step: forward+ReLU-bwd+dX on {rows} of {M_GLOBAL} rows, dW on {wrows} of "
+              f"{N_DIM} rows reducing over {Mw} of {M_GLOBAL} batch rows; FLOP rate scaled to TFLOP/s")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": M_GLOBAL, "N": N_DIM, "K": K_DIM,
+                       "parallelism": "host threads", "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline(seconds_target: float = 10.0):
+    """Oracle forward rows on all host threads (rank 0, N=1): TFLOP/s of the reference's
+    arithmetic on this host. Bounded to roughly `seconds_target` of CPU work."""
+    import numpy as np
+    import oracle
+    threads = oracle.default_threads()
+    rng = np.random.default_rng(1)
+    W = rng.standard_normal((N_DIM, K_DIM), dtype=np.float32) * 0.02
+    b = rng.standard_normal(N_DIM, dtype=np.float32) * 0.01
+    rows = threads
+    X = rng.standard_normal((rows, K_DIM), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.region_fwd(X, W, b, transB=True, threads=threads)
+    dt = time.perf_counter() - t0
+    reps = max(1, min(20, int(seconds_target / max(dt, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.region_fwd(X, W, b, transB=True, threads=threads)
+    dt = time.perf_counter() - t0
+    value = 2.0 * rows * N_DIM * K_DIM * reps / dt / 1e12
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{reps} x forward region on {rows} of {M_GLOBAL} rows (N=K=4096), "
+                      f"sequential-k fp32 as the reference JIT lowers it"}
+
+
+# --------------------------------------------------------------------------- C3 B200 arm
+def run_c3(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _dist_env()
+    if args.gpus != world and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    import c3_b200
+    from c3_b200 import linear
+    L = c3_b200.load()
+    c3_b200.device_check()
+
+    M = M_GLOBAL // world
+    N, K = N_DIM, K_DIM
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    X = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    W = (torch.randn((N, K), generator=torch.Generator(device=dev).manual_seed(99), device=dev)
+         * 0.02).to(torch.bfloat16)
+    b = torch.randn((N,), generator=torch.Generator(device=dev).manual_seed(98), device=dev) * 0.01
+    dY = (torch.randn((M, N), generator=g, device=dev) * 1e-3).to(torch.bfloat16)
+    Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
+    dZ = torch.empty_like(dY)
+    grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)  # packed [dW | db]
+    dW = grads[: N * K].view(N, K)
+    db = grads[N * K:]
+    dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+
+    comp = torch.cuda.current_stream(dev)
+    comm = torch.cuda.Stream(dev)
+    ev_dw_done = torch.cuda.Event()
+    ev_ar_done = torch.cuda.Event()
+    kinds = ("fwd", "prepass", "dw", "dx")
+    kernel_events = {k: [] for k in kinds}
+
+    def step(record: bool):
+        evs = {}
+        def mark(name):
+            if record:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(comp)
+                evs.setdefault(name, []).append(e)
+        mark("fwd"); linear.forward(X, W, b, "nk", Y, mask); mark("fwd")
+        mark("prepass"); linear.relu_mask_db(dY, mask, dZ, db); mark("prepass")
+        mark("dw"); linear.grad_weight(dZ, X, "nk", dW); mark("dw")
+        if world > 1:
+            ev_dw_done.record(comp)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_dw_done)
+                dist.all_reduce(grads)
+                ev_ar_done.record(comm)
+        mark("dx"); linear.grad_input(dZ, W, "nk", dX); mark("dx")
+        if world > 1:
+            comp.wait_event(ev_ar_done)
+        if record:
+            for k in kinds:
+                kernel_events[k].append((evs[k][0], evs[k][1]))
+
+    for _ in range(max(args.warmup, 0)):
+        step(False)
+    torch.cuda.synchronize()
+    c3_b200.fault_status()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        t_start.record(comp)
+        for _ in range(args.steps):
+            step(True)
+        t_end.record(comp)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    c3_b200.fault_status()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    flops_step = 3 * 2.0 * M_GLOBAL * N * K
+    value = flops_step / (ms_per_step * 1e-3) / 1e12
+
+    # per-kernel device time (this rank), for the roofline of the dominant kernel
+    ktime = {k: sum(a.elapsed_time(bv) for a, bv in kernel_events[k]) / args.steps for k in kinds}
+    gemm_ms = ktime["fwd"] + ktime["dw"] + ktime["dx"]
+    gemm_flops = 3 * 2.0 * M * N * K
+    peak_burst, peak_sust, hbm, peak_kind = _peaks()
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    traffic = _traffic()
+
+    # ------------------------------------------------------------------ e2e (host buffers)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": M_GLOBAL, "rows_per_gpu": M,
+                       "N": N, "K": K, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (X, dY 128 MiB each at N=1)",
+                       "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
+                               + (", NCCL all-reduce [dW|db] overlapped with dX" if world > 1 else "")},
+            "frac_of_peak": value / world / peak_sust,
+            "kernel_ms": ktime,
+            "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",
+                         "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                         "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} sustained",
+                         "frac_of_burst": achieved / peak_burst,
+                         "traffic": traffic.get("bytes_per_launch") if traffic else None},
+            "gpu_launches": 4 * args.steps,
+            "clocks": sampler.record(),
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L):
+    """The same step through the C ABI with host (pinned) buffers: every step copies the
+    step's inputs host->device and the results device->host inside the timed region."""
+    import torch
+    import torch.distributed as dist
+    from c3_b200 import linear
+    M, K = X.shape
+    N = W.shape[0]
+    hX = torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True); hX.copy_(X)
+    hdY = torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True); hdY.copy_(dY)
+    hW = torch.empty((N, K), dtype=torch.bfloat16, pin_memory=True); hW.copy_(W)
+    hb = torch.empty((N,), dtype=torch.float32, pin_memory=True); hb.copy_(b)
+    hY = torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True)
+    hdX = torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True)
+    hgrads = torch.empty(N * K + N, dtype=torch.float32, pin_memory=True)
+    dXd, dWd = torch.empty_like(X), torch.empty_like(W)
+    Xd, dYd, bd = torch.empty_like(X), torch.empty_like(dY), torch.empty_like(b)
+    Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
+    dZ = torch.empty_like(dY)
+    grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
+    dW = grads[: N * K].view(N, K)
+    db = grads[N * K:]
+    dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    h2d = hX.numel() * 2 + hdY.numel() * 2 + hW.numel() * 2 + hb.numel() * 4
+    d2h = hY.numel() * 2 + hdX.numel() * 2 + hgrads.numel() * 4
+
+    def step():
+        Xd.copy_(hX, non_blocking=True); dWd.copy_(hW, non_blocking=True)
+        bd.copy_(hb, non_blocking=True)
+        linear.forward(Xd, dWd, bd, "nk", Y, mask)
+        dYd.copy_(hdY, non_blocking=True)
+        hY.copy_(Y, non_blocking=True)
+        linear.relu_mask_db(dYd, mask, dZ, db)
+        linear.grad_weight(dZ, Xd, "nk", dW)
+        if world > 1:
+            dist.all_reduce(grads)
+        linear.grad_input(dZ, dWd, "nk", dX)
+        hdX.copy_(dX, non_blocking=True)
+        hgrads.copy_(grads, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, 10))
+    s.record(comp)
+    for _ in range(steps):
+        step()
+    e.record(comp)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flops = 3 * 2.0 * M_GLOBAL * N * K
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "path": "c3_b200.linear (C ABI) with pinned host buffers, copies on the compute stream"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["c3", "reference"], default="c3")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_c3(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

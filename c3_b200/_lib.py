@@ -1,0 +1,103 @@
+"""Loads libc3cu.so (the C-ABI of include/c3cu.h) and declares its signatures.
+
+The product path has no fallback: if the library is missing and cannot be built, or if
+the current device is not an sm_100 part, every entry point raises C3CUError."""
+from __future__ import annotations
+
+import ctypes
+import re
+import threading
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libc3cu.so"
+HEADERS = [PKG.parent / "include" / "c3cu.h"]
+
+OK = 0
+ERR_NAMES = {-1: "INVALID", -2: "ALIGN", -3: "CUDA", -4: "FAULT", -5: "UNSUPPORTED",
+             -6: "WORKSPACE"}
+
+W_NK, W_KN = 0, 1
+EPI_BIAS_RELU_MASK, EPI_STORE_BF16, EPI_STORE_F32, EPI_BIAS_STORE_F32 = 0, 1, 2, 3
+
+
+class C3CUError(RuntimeError):
+    def __init__(self, code: int, where: str, message: str):
+        self.code = code
+        super().__init__(f"{where}: C3CU_ERR_{ERR_NAMES.get(code, code)} ({code}): {message}")
+
+
+_lock = threading.Lock()
+_lib = None
+
+_vp, _i64, _i, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+
+_SIGNATURES = {
+    "c3cu_version": ([], _i),
+    "c3cu_last_error": ([], ctypes.c_char_p),
+    "c3cu_device_check": ([], _i),
+    "c3cu_fault_status": ([ctypes.POINTER(ctypes.c_uint32)], _i),
+    "c3cu_linear_bias_relu_fwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _vp], _i),
+    "c3cu_relu_mask_db_workspace": ([_i64, _i64], _sz),
+    "c3cu_relu_mask_db": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp, _sz, _vp], _i),
+    "c3cu_gemm_dx": ([_vp, _vp, _vp, _i64, _i64, _i64, _i, _vp], _i),
+    "c3cu_gemm_dw": ([_vp, _vp, _vp, _i64, _i64, _i64, _i, _vp], _i),
+    "c3cu_gemm_bf16": ([_vp, _i64, _i, _vp, _i64, _i, _vp, _i64, _i, _vp, _vp, _i64, _i64, _i64,
+                        _i64, _vp], _i),
+    "c3cu_ew_chain_cfg4": ([_vp, _vp, _vp, _vp, _i64, _vp], _i),
+    "c3cu_ew_program": ([_vp, _vp, _i, _vp, _i, _vp, _i, _i, _vp, _i64, _vp], _i),
+    "c3cu_sum_rows_f32_workspace": ([_i64, _i64], _sz),
+    "c3cu_sum_rows_f32": ([_vp, _vp, _i64, _i64, _vp, _sz, _vp], _i),
+}
+
+
+def declared_symbols() -> list[str]:
+    """Every function name declared in include/*.h (used by the export test)."""
+    names = []
+    for h in sorted((PKG.parent / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        names += re.findall(r"\b(c3\w*)\s*\(", text)
+    return sorted(set(n for n in names if not n.isupper()))
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            if not build_if_missing:
+                raise RuntimeError(f"{LIB_PATH} is missing; build it with `python -m c3_b200.build`")
+            from . import build as _build
+            _build.build()
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+        return L
+
+
+def last_error() -> str:
+    msg = load().c3cu_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, where: str) -> None:
+    if rc != OK:
+        raise C3CUError(rc, where, last_error())
+
+
+def device_check() -> None:
+    check(load().c3cu_device_check(), "c3cu_device_check")
+
+
+def fault_status() -> int:
+    """Synchronises the device and returns (and clears) the kernels' fault word; raises
+    C3CUError(C3CU_ERR_FAULT) when a kernel recorded a fault."""
+    code = ctypes.c_uint32(0)
+    rc = load().c3cu_fault_status(ctypes.byref(code))
+    check(rc, "c3cu_fault_status")
+    return code.value

@@ -1,0 +1,421 @@
+// HBM-bound kernels of the C3 hot path (include/c3cu.h):
+//   * c3cu_relu_mask_db   — ReLU backward dZ = float(mask) * dY fused with the Add-backward
+//                           column sum db = sum_rows dZ (deterministic two-level reduction)
+//   * c3cu_sum_rows_f32   — SumReduce axis 0 over an fp32 matrix
+//   * c3cu_ew_chain_cfg4  — relu((A + B) * C - A) / (1 + exp(-B)) in one pass
+//   * c3cu_ew_program     — general single-pass elementwise chain (register-machine program)
+//
+// All of them stream with 128-bit loads/stores, coalesced across each warp, and size the
+// grid as a multiple of the SM count. Floating-point operations are written with the
+// explicit round-to-nearest intrinsics (__fadd_rn, __fmul_rn, ...) so that the compiler
+// cannot contract them into FMAs: the reference evaluates each node as a separate fp32
+// operation (src/C3/MLIRKernelGen.cpp:394-768), and the kernels keep that order.
+#include <vector>
+
+#include "common.cuh"
+#include "host_util.h"
+
+C3CU_FAULT_ACCESSORS(ew)
+
+namespace c3cu {
+namespace ew {
+
+constexpr int kColsPerWarp = 256;   // 32 lanes x 8 columns
+constexpr int kWarps = 8;
+constexpr int kRowsPerBlock = 512;  // rows one block reduces before the cross-block pass
+
+// ------------------------------------------------------------------ column sums
+// One block covers a strip of 256 columns and up to 512 rows. Each thread owns 8 adjacent
+// columns; warps stride over rows. The block writes its 256 partial sums to
+// `partials[row_block][col]`; the last block of a strip to finish (atomic ticket) adds the
+// partials of that strip in row-block order, so the result does not depend on scheduling.
+//
+// MASKED: input bf16 dY with a bit-packed mask; also writes dZ = float(bit) * dY as bf16
+//         (reference: Mul(Gt(x, 0), grad), src/C3/C3BackwardCapture.cpp:501-528, where
+//         Gt yields 1.0f / 0.0f, src/C3/MLIRKernelGen.cpp:173-211).
+// !MASKED: input fp32, sum only (SumReduce axis 0, src/C3/C3DialectLowering.cpp:382-465).
+template <bool MASKED>
+__global__ void __launch_bounds__(kWarps * 32)
+    colsum_kernel(const void* __restrict__ in, const uint32_t* __restrict__ mask,
+                  __nv_bfloat16* __restrict__ dz, float* __restrict__ out, int M, int N,
+                  int ldm, float* __restrict__ partials, unsigned int* __restrict__ tickets,
+                  int vec_ok) {
+  __shared__ float red[kWarps][kColsPerWarp];
+  __shared__ bool is_last;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int strip = blockIdx.x;
+  const int rb = blockIdx.y;
+  const int col = strip * kColsPerWarp + lane * 8;
+  const int row0 = rb * kRowsPerBlock;
+  const int row1 = min(M, row0 + kRowsPerBlock);
+
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+
+  if (col < N) {
+    const bool vec = vec_ok && (col + 8 <= N);
+#pragma unroll 4
+    for (int r = row0 + warp; r < row1; r += kWarps) {
+      float v[8];
+      if constexpr (MASKED) {
+        const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in) + (int64_t)r * N + col;
+        uint32_t raw[4];
+        if (vec) {
+          const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
+          raw[0] = q.x; raw[1] = q.y; raw[2] = q.z; raw[3] = q.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = (col + 2 * j < N) ? __bfloat16_as_ushort(src[2 * j]) : 0u;
+            const uint32_t hi = (col + 2 * j + 1 < N) ? __bfloat16_as_ushort(src[2 * j + 1]) : 0u;
+            raw[j] = lo | (hi << 16);
+          }
+        }
+        const uint32_t word = __ldg(mask + (int64_t)r * ldm + (col >> 5));
+        const uint32_t bits = word >> (col & 31);
+        uint32_t outw[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float g0 = __uint_as_float(raw[j] << 16);
+          const float g1 = __uint_as_float(raw[j] & 0xffff0000u);
+          v[2 * j] = __fmul_rn((bits >> (2 * j)) & 1u ? 1.f : 0.f, g0);
+          v[2 * j + 1] = __fmul_rn((bits >> (2 * j + 1)) & 1u ? 1.f : 0.f, g1);
+          // v is exactly g or a signed zero, so the bf16 repacking is exact.
+          outw[j] = (__float_as_uint(v[2 * j]) >> 16) | (__float_as_uint(v[2 * j + 1]) & 0xffff0000u);
+        }
+        __nv_bfloat16* dst = dz + (int64_t)r * N + col;
+        if (vec) {
+          __stcs(reinterpret_cast<uint4*>(dst), make_uint4(outw[0], outw[1], outw[2], outw[3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (col + j < N)
+              dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(outw[j >> 1] >> (16 * (j & 1))));
+        }
+      } else {
+        const float* src = static_cast<const float*>(in) + (int64_t)r * N + col;
+        if (vec) {
+          const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+          const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = (col + j < N) ? src[j] : 0.f;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+    }
+  }
+
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  // thread t adds column t of the strip over the 8 warps, in warp order
+  const int t = threadIdx.x;
+  const int c = strip * kColsPerWarp + t;
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, red[w][t]);
+  if (c < N) partials[(int64_t)rb * N + c] = s;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    const unsigned int ticket = atomicAdd(&tickets[strip], 1u);
+    is_last = (ticket == gridDim.y - 1);
+  }
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    if (c < N) {
+      float tot = 0.f;
+      for (int b = 0; b < static_cast<int>(gridDim.y); ++b)
+        tot = __fadd_rn(tot, __ldcg(partials + (int64_t)b * N + c));
+      out[c] = tot;
+    }
+    if (t == 0) tickets[strip] = 0u;  // re-arm for the next launch on this workspace
+  }
+}
+
+size_t colsum_workspace(int64_t M, int64_t N) {
+  const int64_t rbs = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
+  const size_t partial_bytes = static_cast<size_t>(rbs > 0 ? rbs : 1) * static_cast<size_t>(N) * 4u;
+  const size_t ticket_bytes = static_cast<size_t>(strips > 0 ? strips : 1) * 4u;
+  return ((partial_bytes + 255u) & ~static_cast<size_t>(255u)) + ticket_bytes;
+}
+
+template <bool MASKED>
+int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, int64_t M, int64_t N,
+                  void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (M < 0 || N < 0 || M > INT32_MAX || N > INT32_MAX) {
+    set_error("column sum: sizes out of range");
+    return C3CU_ERR_INVALID;
+  }
+  if (N == 0) return C3CU_OK;
+  if (!out || (M > 0 && !in) || (MASKED && M > 0 && (!mask || !dz))) {
+    set_error("column sum: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  if (M == 0) {
+    // Empty reduction: every column sums to +0.
+    return cuda_status(cudaMemsetAsync(out, 0, static_cast<size_t>(N) * 4u, st), "column sum: zero");
+  }
+  const size_t need = colsum_workspace(M, N);
+  if (!ws || ws_bytes < need) {
+    set_error("column sum: workspace of %zu bytes needed, %zu given", need, ws ? ws_bytes : 0);
+    return C3CU_ERR_WORKSPACE;
+  }
+  const int64_t rbs = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
+  if (rbs > 65535) {
+    set_error("column sum: M=%lld exceeds %lld rows", (long long)M, (long long)65535 * kRowsPerBlock);
+    return C3CU_ERR_INVALID;
+  }
+  float* partials = static_cast<float*>(ws);
+  const size_t partial_bytes = static_cast<size_t>(rbs) * static_cast<size_t>(N) * 4u;
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(
+      static_cast<uint8_t*>(ws) + ((partial_bytes + 255u) & ~static_cast<size_t>(255u)));
+  int rc = cuda_status(cudaMemsetAsync(tickets, 0, static_cast<size_t>(strips) * 4u, st),
+                       "column sum: reset tickets");
+  if (rc != C3CU_OK) return rc;
+  const int esize = MASKED ? 2 : 4;
+  const int vec_ok = aligned16(in) && (!MASKED || aligned16(dz)) && ((N * esize) % 16 == 0);
+  const int ldm = static_cast<int>((N + 31) / 32);
+  dim3 grid(static_cast<unsigned>(strips), static_cast<unsigned>(rbs));
+  colsum_kernel<MASKED><<<grid, kWarps * 32, 0, st>>>(in, mask, static_cast<__nv_bfloat16*>(dz), out,
+                                                     static_cast<int>(M), static_cast<int>(N), ldm,
+                                                     partials, tickets, vec_ok);
+  return cuda_status(cudaGetLastError(), "column sum: launch");
+}
+
+// ------------------------------------------------------------------ cfg4 chain
+__device__ __forceinline__ float chain_cfg4(float a, float b, float c) {
+  // Graph order of relu((A + B) * C - A) / (1 + exp(-B)): FusedNode [Add, Mul, Sub, ReLU, Div]
+  // with the divisor 1 + exp(-B) computed by the separate Neg, Exp, Add nodes.
+  const float s = __fadd_rn(a, b);
+  const float m = __fmul_rn(s, c);
+  const float t = __fsub_rn(m, a);
+  const float r = fmaxf(t, 0.f);
+  const float d = __fadd_rn(1.f, expf(-b));
+  return __fdiv_rn(r, d);
+}
+
+__global__ void __launch_bounds__(256)
+    chain_cfg4_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                      const float* __restrict__ C, float* __restrict__ out, int64_t n, int vec_ok) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (vec_ok) {
+    const int64_t n4 = n >> 2;
+    const float4* A4 = reinterpret_cast<const float4*>(A);
+    const float4* B4 = reinterpret_cast<const float4*>(B);
+    const float4* C4 = reinterpret_cast<const float4*>(C);
+    float4* O4 = reinterpret_cast<float4*>(out);
+    int64_t i = tid;
+    // two float4 per thread per iteration: 6 independent 16-byte loads in flight
+    for (; i + nthreads < n4; i += 2 * nthreads) {
+      const float4 a0 = __ldcs(A4 + i), b0 = __ldcs(B4 + i), c0 = __ldcs(C4 + i);
+      const float4 a1 = __ldcs(A4 + i + nthreads), b1 = __ldcs(B4 + i + nthreads),
+                   c1 = __ldcs(C4 + i + nthreads);
+      __stcs(O4 + i, make_float4(chain_cfg4(a0.x, b0.x, c0.x), chain_cfg4(a0.y, b0.y, c0.y),
+                                 chain_cfg4(a0.z, b0.z, c0.z), chain_cfg4(a0.w, b0.w, c0.w)));
+      __stcs(O4 + i + nthreads,
+             make_float4(chain_cfg4(a1.x, b1.x, c1.x), chain_cfg4(a1.y, b1.y, c1.y),
+                         chain_cfg4(a1.z, b1.z, c1.z), chain_cfg4(a1.w, b1.w, c1.w)));
+    }
+    for (; i < n4; i += nthreads) {
+      const float4 a = __ldcs(A4 + i), b = __ldcs(B4 + i), c = __ldcs(C4 + i);
+      __stcs(O4 + i, make_float4(chain_cfg4(a.x, b.x, c.x), chain_cfg4(a.y, b.y, c.y),
+                                 chain_cfg4(a.z, b.z, c.z), chain_cfg4(a.w, b.w, c.w)));
+    }
+    for (int64_t k = (n4 << 2) + tid; k < n; k += nthreads) out[k] = chain_cfg4(A[k], B[k], C[k]);
+  } else {
+    for (int64_t k = tid; k < n; k += nthreads) out[k] = chain_cfg4(A[k], B[k], C[k]);
+  }
+}
+
+// ------------------------------------------------------------------ general chain
+struct Program {
+  const float* in[C3CU_EW_MAX_INPUTS];
+  int64_t numel[C3CU_EW_MAX_INPUTS];
+  uint32_t code[C3CU_EW_MAX_INSTR];  // {op, dst, src0, src1} packed little-endian
+  float consts[16];
+  int n_inputs;
+  int n_instr;
+  int out_reg;
+};
+
+__device__ __forceinline__ float ew_apply(uint32_t op, float a, float b, float cst) {
+  switch (op) {
+    case C3CU_EW_ADD: return __fadd_rn(a, b);
+    case C3CU_EW_SUB: return __fsub_rn(a, b);
+    case C3CU_EW_MUL: return __fmul_rn(a, b);
+    case C3CU_EW_DIV: return __fdiv_rn(a, b);
+    case C3CU_EW_DIV_NANZ: return b == 0.f ? __int_as_float(0x7fc00000) : __fdiv_rn(a, b);
+    case C3CU_EW_NEG: return -a;
+    case C3CU_EW_RELU: return fmaxf(a, 0.f);
+    case C3CU_EW_EXP: return expf(a);
+    case C3CU_EW_LOG: return logf(a);
+    case C3CU_EW_SIGMOID: return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-a)));
+    case C3CU_EW_TANH: return tanhf(a);
+    case C3CU_EW_TANH_EXP: {
+      const float ep = expf(a), en = expf(-a);
+      return __fdiv_rn(__fsub_rn(ep, en), __fadd_rn(ep, en));
+    }
+    case C3CU_EW_GT: return a > b ? 1.f : 0.f;
+    case C3CU_EW_CONST: return cst;
+    case C3CU_EW_MOV: return a;
+    default: return __int_as_float(0x7fc00000);
+  }
+}
+
+// Registers live in a per-thread array; each thread evaluates the program on 4 adjacent
+// elements so that every decoded instruction is amortised over a 128-bit vector.
+__global__ void __launch_bounds__(256) program_kernel(const Program prog, float* __restrict__ out,
+                                                      int64_t n) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = tid * 4; base < n; base += nthreads * 4) {
+    float reg[16][4];
+    const bool full = base + 4 <= n;
+    for (int i = 0; i < prog.n_inputs; ++i) {
+      const float* p = prog.in[i];
+      const int64_t ne = prog.numel[i];
+      if (ne == n && full && ((reinterpret_cast<uintptr_t>(p + base) & 15u) == 0u)) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(p + base));
+        reg[i][0] = v.x; reg[i][1] = v.y; reg[i][2] = v.z; reg[i][3] = v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t idx = base + e;
+          reg[i][e] = (idx < n) ? __ldg(p + (ne == n ? idx : idx % ne)) : 0.f;
+        }
+      }
+    }
+    for (int k = 0; k < prog.n_instr; ++k) {
+      const uint32_t w = prog.code[k];
+      const uint32_t op = w & 0xffu, dst = (w >> 8) & 0xfu, s0 = (w >> 16) & 0xfu, s1 = (w >> 24) & 0xfu;
+      const float cst = prog.consts[s0];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) reg[dst][e] = ew_apply(op, reg[s0][e], reg[s1][e], cst);
+    }
+    const int o = prog.out_reg;
+    if (full && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0u)) {
+      __stcs(reinterpret_cast<float4*>(out + base), make_float4(reg[o][0], reg[o][1], reg[o][2], reg[o][3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (base + e < n) out[base + e] = reg[o][e];
+    }
+  }
+}
+
+int grid_for(int64_t work_items, int threads) {
+  const int64_t sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t want = (work_items + threads - 1) / threads;
+  const int64_t cap = sms * 8;  // 8 resident 256-thread blocks per SM
+  int64_t g = want < cap ? want : cap;
+  return static_cast<int>(g > 0 ? g : 1);
+}
+
+}  // namespace ew
+}  // namespace c3cu
+
+extern "C" {
+
+size_t c3cu_relu_mask_db_workspace(int64_t M, int64_t N) { return c3cu::ew::colsum_workspace(M, N); }
+
+int c3cu_relu_mask_db(const void* dY, const uint32_t* mask, void* dZ, float* db, int64_t M,
+                      int64_t N, void* workspace, size_t workspace_bytes, c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  return c3cu::ew::launch_colsum<true>(dY, mask, dZ, db, M, N, workspace, workspace_bytes,
+                                       static_cast<cudaStream_t>(stream));
+}
+
+size_t c3cu_sum_rows_f32_workspace(int64_t M, int64_t N) { return c3cu::ew::colsum_workspace(M, N); }
+
+int c3cu_sum_rows_f32(const float* in, float* out, int64_t M, int64_t N, void* workspace,
+                      size_t workspace_bytes, c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  return c3cu::ew::launch_colsum<false>(in, nullptr, nullptr, out, M, N, workspace,
+                                        workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* out, int64_t n,
+                       c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (n < 0) {
+    c3cu::set_error("ew_chain_cfg4: negative size");
+    return C3CU_ERR_INVALID;
+  }
+  if (n == 0) return C3CU_OK;
+  if (!A || !B || !C || !out) {
+    c3cu::set_error("ew_chain_cfg4: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  const int vec_ok = c3cu::aligned16(A) && c3cu::aligned16(B) && c3cu::aligned16(C) &&
+                     c3cu::aligned16(out);
+  const int grid = c3cu::ew::grid_for((n + 7) / 8, 256);
+  c3cu::ew::chain_cfg4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(A, B, C, out, n,
+                                                                                   vec_ok);
+  return c3cu::cuda_status(cudaGetLastError(), "ew_chain_cfg4: launch");
+}
+
+int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,
+                    const uint8_t* code, int n_instr, const float* constants, int n_constants,
+                    int out_reg, float* out, int64_t n, c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (n < 0 || n_inputs < 0 || n_inputs > C3CU_EW_MAX_INPUTS || n_instr < 0 ||
+      n_instr > C3CU_EW_MAX_INSTR || n_constants < 0 || n_constants > 16 || out_reg < 0 ||
+      out_reg > 15) {
+    c3cu::set_error("ew_program: bad program shape (inputs %d, instructions %d, constants %d)",
+                    n_inputs, n_instr, n_constants);
+    return C3CU_ERR_INVALID;
+  }
+  if (n == 0) return C3CU_OK;
+  if (!out || (n_inputs > 0 && (!inputs || !numels)) || (n_instr > 0 && !code)) {
+    c3cu::set_error("ew_program: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::ew::Program prog{};
+  prog.n_inputs = n_inputs;
+  prog.n_instr = n_instr;
+  prog.out_reg = out_reg;
+  for (int i = 0; i < n_inputs; ++i) {
+    if (!inputs[i] || numels[i] <= 0) {
+      c3cu::set_error("ew_program: input %d is null or empty", i);
+      return C3CU_ERR_INVALID;
+    }
+    if (numels[i] != n && n % numels[i] != 0 && numels[i] > n) {
+      c3cu::set_error("ew_program: input %d has %lld elements, output %lld", i,
+                      (long long)numels[i], (long long)n);
+      return C3CU_ERR_INVALID;
+    }
+    prog.in[i] = inputs[i];
+    prog.numel[i] = numels[i];
+  }
+  for (int k = 0; k < n_instr; ++k) {
+    const uint8_t op = code[4 * k], dst = code[4 * k + 1], s0 = code[4 * k + 2], s1 = code[4 * k + 3];
+    if (op < C3CU_EW_ADD || op > C3CU_EW_MOV || dst > 15 || s0 > 15 || s1 > 15 ||
+        (op == C3CU_EW_CONST && s0 >= n_constants)) {
+      c3cu::set_error("ew_program: bad instruction %d {%u,%u,%u,%u}", k, op, dst, s0, s1);
+      return C3CU_ERR_INVALID;
+    }
+    prog.code[k] = static_cast<uint32_t>(op) | (static_cast<uint32_t>(dst) << 8) |
+                   (static_cast<uint32_t>(s0) << 16) | (static_cast<uint32_t>(s1) << 24);
+  }
+  for (int c = 0; c < n_constants; ++c) prog.consts[c] = constants[c];
+  const int grid = c3cu::ew::grid_for((n + 3) / 4, 256);
+  c3cu::ew::program_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(prog, out, n);
+  return c3cu::cuda_status(cudaGetLastError(), "ew_program: launch");
+}
+
+}  // extern "C"

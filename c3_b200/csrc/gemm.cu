@@ -1,0 +1,172 @@
+// C-ABI entry points of the tcgen05 GEMM family (include/c3cu.h): the fused
+// Linear+bias+ReLU forward, the dX / dW backward GEMMs and the general bf16 GEMM.
+#include "gemm_tcgen05.cuh"
+#include "host_util.h"
+
+C3CU_FAULT_ACCESSORS(gemm)
+
+namespace c3cu {
+namespace {
+
+using gemm::Params;
+
+template <bool A_MN, bool B_MN, int EPI>
+int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
+           cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  int rc;
+  // A tile: 128 (M) x 64 (K). K-major: one box {64 K, 128 rows}; MN-major: boxes {64 M, 64 K}.
+  if (!A_MN)
+    rc = encode_bf16_2d_sw128(&ta, A, p.M, p.K, lda, 64, gemm::BM);
+  else
+    rc = encode_bf16_2d_sw128(&ta, A, p.K, p.M, lda, 64, gemm::BK);
+  if (rc != C3CU_OK) return rc;
+  // B tile: 256 (N) x 64 (K).
+  if (!B_MN)
+    rc = encode_bf16_2d_sw128(&tb, B, p.N, p.K, ldb, 64, gemm::BN);
+  else
+    rc = encode_bf16_2d_sw128(&tb, B, p.K, p.N, ldb, 64, gemm::BK);
+  if (rc != C3CU_OK) return rc;
+
+  auto kern = gemm::gemm_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set = false;  // per instantiation; idempotent, so a race is harmless
+  if (!attr_set) {
+    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          gemm::SMEM_BYTES),
+                     "gemm: set max dynamic shared memory");
+    if (rc != C3CU_OK) return rc;
+    attr_set = true;
+  }
+  const int tiles = ((p.M + gemm::BM - 1) / gemm::BM) * ((p.N + gemm::BN - 1) / gemm::BN);
+  const int sms = sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, gemm::kThreads, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
+  return cuda_status(cudaGetLastError(), "gemm: launch");
+}
+
+int dispatch(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+             int epi, const Params& p, cudaStream_t st) {
+#define C3CU_GEMM_CASE(AM, BMN, E) \
+  if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, st);
+  C3CU_GEMM_CASE(0, 0, kEpiBiasReluMask)
+  C3CU_GEMM_CASE(0, 1, kEpiBiasReluMask)
+  C3CU_GEMM_CASE(0, 0, kEpiStoreBf16)
+  C3CU_GEMM_CASE(0, 1, kEpiStoreBf16)
+  C3CU_GEMM_CASE(1, 1, kEpiStoreF32)
+  C3CU_GEMM_CASE(0, 0, kEpiStoreF32)
+  C3CU_GEMM_CASE(0, 1, kEpiStoreF32)
+  C3CU_GEMM_CASE(1, 0, kEpiStoreF32)
+  C3CU_GEMM_CASE(0, 0, kEpiBiasStoreF32)
+  C3CU_GEMM_CASE(0, 1, kEpiBiasStoreF32)
+#undef C3CU_GEMM_CASE
+  set_error("gemm: no kernel instantiated for a_mn=%d b_mn=%d epilogue=%d", a_mn, b_mn, epi);
+  return C3CU_ERR_INVALID;
+}
+
+int check_common(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) {
+    set_error("gemm: sizes out of range M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+              (long long)K);
+    return C3CU_ERR_INVALID;
+  }
+  if (K == 0 && M > 0 && N > 0) {
+    set_error("gemm: K == 0 is not supported (empty reduction)");
+    return C3CU_ERR_INVALID;
+  }
+  return require_sm100();
+}
+
+}  // namespace
+
+int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                 void* out, int64_t ldo, int epi, const float* bias, uint32_t* mask, int64_t ldm,
+                 int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  int rc = check_common(M, N, K);
+  if (rc != C3CU_OK) return rc;
+  if (M == 0 || N == 0) return C3CU_OK;
+  if (!A || !B || !out) {
+    set_error("gemm: null operand");
+    return C3CU_ERR_INVALID;
+  }
+  const bool bias_epi = (epi == kEpiBiasReluMask || epi == kEpiBiasStoreF32);
+  if (bias_epi && !bias) {
+    set_error("gemm: epilogue %d needs a bias", epi);
+    return C3CU_ERR_INVALID;
+  }
+  if (epi == kEpiBiasReluMask && (!mask || ldm < (N + 31) / 32)) {
+    set_error("gemm: ReLU-mask epilogue needs a mask with ldm >= ceil(N/32)");
+    return C3CU_ERR_INVALID;
+  }
+  if (ldo < N) {
+    set_error("gemm: output row stride %lld < N %lld", (long long)ldo, (long long)N);
+    return C3CU_ERR_INVALID;
+  }
+  Params p;
+  p.M = static_cast<int32_t>(M);
+  p.N = static_cast<int32_t>(N);
+  p.K = static_cast<int32_t>(K);
+  p.out = out;
+  p.ldo = ldo;
+  p.bias = bias;
+  p.mask = mask;
+  p.ldm = ldm;
+  const int esize = (epi == kEpiStoreF32 || epi == kEpiBiasStoreF32) ? 4 : 2;
+  p.vec_ok = aligned16(out) && ((ldo * esize) % 16 == 0) &&
+             (!bias_epi || aligned16(bias)) ? 1 : 0;
+  return dispatch(A, lda, a_mn, B, ldb, b_mn, epi, p, st);
+}
+
+}  // namespace c3cu
+
+extern "C" {
+
+int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                   void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,
+                   int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream) {
+  return c3cu::gemm_general(A, lda, a_mn, B, ldb, b_mn, out, ldo, epilogue, bias, mask, ldm, M,
+                            N, K, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_linear_bias_relu_fwd(const void* X, const void* W, const float* bias, void* Y,
+                              uint32_t* mask, int64_t M, int64_t N, int64_t K, int w_layout,
+                              c3cu_stream_t stream) {
+  if (w_layout != C3CU_W_NK && w_layout != C3CU_W_KN) {
+    c3cu::set_error("linear_bias_relu_fwd: unknown weight layout %d", w_layout);
+    return C3CU_ERR_INVALID;
+  }
+  // Y[M][N] = X[M][K] * W[N][K]^T  (W K-major)  or  X[M][K] * B[K][N]  (B MN-major)
+  const int64_t ldb = (w_layout == C3CU_W_NK) ? K : N;
+  return c3cu::gemm_general(X, K, 0, W, ldb, w_layout == C3CU_W_KN ? 1 : 0, Y, N,
+                            c3cu::kEpiBiasReluMask, bias, mask, (N + 31) / 32, M, N, K,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_gemm_dx(const void* dZ, const void* W, void* dX, int64_t M, int64_t N, int64_t K,
+                 int w_layout, c3cu_stream_t stream) {
+  // dX[M][K] = dZ[M][N] * W[N][K]  -> GEMM (M, K, red N): A = dZ K-major, B = W stored [N][K]
+  // (reduction-major = MN-major). With B[K][N]: dX = dZ * B^T, B stored [K][N] = K-major.
+  if (w_layout == C3CU_W_NK)
+    return c3cu::gemm_general(dZ, N, 0, W, K, 1, dX, K, c3cu::kEpiStoreBf16, nullptr, nullptr, 0,
+                              M, K, N, static_cast<cudaStream_t>(stream));
+  if (w_layout == C3CU_W_KN)
+    return c3cu::gemm_general(dZ, N, 0, W, N, 0, dX, K, c3cu::kEpiStoreBf16, nullptr, nullptr, 0,
+                              M, K, N, static_cast<cudaStream_t>(stream));
+  c3cu::set_error("gemm_dx: unknown weight layout %d", w_layout);
+  return C3CU_ERR_INVALID;
+}
+
+int c3cu_gemm_dw(const void* dZ, const void* X, float* dW, int64_t M, int64_t N, int64_t K,
+                 int w_layout, c3cu_stream_t stream) {
+  // dW[N][K] = dZ^T * X : GEMM (N, K, red M); A = dZ stored [M][N], B = X stored [M][K]
+  // (both MN-major). dB[K][N] = X^T * dZ: the same with the operands swapped.
+  if (w_layout == C3CU_W_NK)
+    return c3cu::gemm_general(dZ, N, 1, X, K, 1, dW, K, c3cu::kEpiStoreF32, nullptr, nullptr, 0,
+                              N, K, M, static_cast<cudaStream_t>(stream));
+  if (w_layout == C3CU_W_KN)
+    return c3cu::gemm_general(X, K, 1, dZ, N, 1, dW, N, c3cu::kEpiStoreF32, nullptr, nullptr, 0,
+                              K, N, M, static_cast<cudaStream_t>(stream));
+  c3cu::set_error("gemm_dw: unknown weight layout %d", w_layout);
+  return C3CU_ERR_INVALID;
+}
+
+}  // extern "C"

@@ -1,0 +1,38 @@
+// Host-side helpers shared by the C-ABI translation units: error reporting, device
+// properties, and TMA descriptor encoding through the driver entry point (the library
+// does not link libcuda directly, so it loads on machines without a GPU driver).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/c3cu.h"
+
+namespace c3cu {
+
+// Records the message returned by c3cu_last_error() for the calling thread.
+void set_error(const char* fmt, ...);
+
+// Returns C3CU_ERR_CUDA (and records the message) when `e` is an error.
+int cuda_status(cudaError_t e, const char* what);
+
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+// C3CU_OK when the current device is an sm_100 part; the kernels carry sm_100a code only.
+int require_sm100();
+
+// Encodes a 2-D tiled tensor map over a row-major bf16 matrix [rows][cols] with row stride
+// `ld` elements, box {box_cols, box_rows} and 128-byte swizzle. Checks the TMA rules
+// (16-byte aligned base and stride) before calling the driver.
+int encode_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                         uint64_t ld, uint32_t box_cols, uint32_t box_rows);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
+
+}  // namespace c3cu

@@ -1,0 +1,146 @@
+"""Fused Linear+bias+ReLU forward and its captured backward on B200 kernels.
+
+Functional wrappers over the C ABI (include/c3cu.h). Tensors are torch CUDA tensors used
+as device memory; every call is launched on torch's current stream of the tensor's
+device. Shapes follow the reference region MatMul+Add+ReLU
+(include/C3/C3HotPathManager.h:521-611): X [M, K], weight W [N, K] ("nk", nn.Linear) or
+B [K, N] ("kn", the reference's MatMul rhs), bias b [N]."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_ws_cache: dict[int, torch.Tensor] = {}
+
+
+def _p(t: torch.Tensor | None):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _layout(w_layout: str) -> int:
+    if w_layout == "nk":
+        return _lib.W_NK
+    if w_layout == "kn":
+        return _lib.W_KN
+    raise ValueError(f"w_layout must be 'nk' or 'kn', got {w_layout!r}")
+
+
+def _require(t: torch.Tensor, name: str, dtype: torch.dtype, ndim: int):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise _lib.C3CUError(-1, name, "expected a CUDA tensor")
+    if t.dtype != dtype or t.dim() != ndim or not t.is_contiguous():
+        raise _lib.C3CUError(-1, name, f"expected contiguous {dtype} with {ndim} dims, got "
+                                       f"{t.dtype} {tuple(t.shape)} contiguous={t.is_contiguous()}")
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _ws_cache.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[idx] = ws
+    return ws
+
+
+def mask_words(n: int) -> int:
+    return (n + 31) // 32
+
+
+def forward(X: torch.Tensor, W: torch.Tensor, b: torch.Tensor, w_layout: str = "nk",
+            Y: torch.Tensor | None = None, mask: torch.Tensor | None = None):
+    """Y = max(X W^T + b, 0) (or X B + b), bf16 out, plus the bit-packed ReLU mask
+    ([M, ceil(N/32)] int32 holding uint32 words)."""
+    lay = _layout(w_layout)
+    _require(X, "X", torch.bfloat16, 2)
+    _require(W, "W", torch.bfloat16, 2)
+    _require(b, "b", torch.float32, 1)
+    M, K = X.shape
+    N = W.shape[0] if lay == _lib.W_NK else W.shape[1]
+    wk = W.shape[1] if lay == _lib.W_NK else W.shape[0]
+    if wk != K or b.numel() != N:
+        raise _lib.C3CUError(-1, "forward", f"shape mismatch X{tuple(X.shape)} W{tuple(W.shape)} "
+                                            f"b{tuple(b.shape)} layout={w_layout}")
+    if Y is None:
+        Y = torch.empty((M, N), dtype=torch.bfloat16, device=X.device)
+    if mask is None:
+        mask = torch.empty((M, mask_words(N)), dtype=torch.int32, device=X.device)
+    rc = _lib.load().c3cu_linear_bias_relu_fwd(_p(X), _p(W), _p(b), _p(Y), _p(mask), M, N, K, lay,
+                                               _stream(X.device))
+    _lib.check(rc, "c3cu_linear_bias_relu_fwd")
+    return Y, mask
+
+
+def relu_mask_db(dY: torch.Tensor, mask: torch.Tensor, dZ: torch.Tensor | None = None,
+                 db: torch.Tensor | None = None):
+    """dZ = float(mask) * dY (bf16, exact) and db = column sums of dZ (fp32)."""
+    _require(dY, "dY", torch.bfloat16, 2)
+    _require(mask, "mask", torch.int32, 2)
+    M, N = dY.shape
+    if dZ is None:
+        dZ = torch.empty_like(dY)
+    if db is None:
+        db = torch.empty(N, dtype=torch.float32, device=dY.device)
+    L = _lib.load()
+    nb = L.c3cu_relu_mask_db_workspace(M, N)
+    ws = workspace(dY.device, nb)
+    rc = L.c3cu_relu_mask_db(_p(dY), _p(mask), _p(dZ), _p(db), M, N, _p(ws), ws.numel(),
+                             _stream(dY.device))
+    _lib.check(rc, "c3cu_relu_mask_db")
+    return dZ, db
+
+
+def grad_input(dZ: torch.Tensor, W: torch.Tensor, w_layout: str = "nk", dX: torch.Tensor | None = None):
+    lay = _layout(w_layout)
+    _require(dZ, "dZ", torch.bfloat16, 2)
+    _require(W, "W", torch.bfloat16, 2)
+    M, N = dZ.shape
+    K = W.shape[1] if lay == _lib.W_NK else W.shape[0]
+    if dX is None:
+        dX = torch.empty((M, K), dtype=torch.bfloat16, device=dZ.device)
+    rc = _lib.load().c3cu_gemm_dx(_p(dZ), _p(W), _p(dX), M, N, K, lay, _stream(dZ.device))
+    _lib.check(rc, "c3cu_gemm_dx")
+    return dX
+
+
+def grad_weight(dZ: torch.Tensor, X: torch.Tensor, w_layout: str = "nk", dW: torch.Tensor | None = None):
+    lay = _layout(w_layout)
+    _require(dZ, "dZ", torch.bfloat16, 2)
+    _require(X, "X", torch.bfloat16, 2)
+    M, N = dZ.shape
+    K = X.shape[1]
+    shape = (N, K) if lay == _lib.W_NK else (K, N)
+    if dW is None:
+        dW = torch.empty(shape, dtype=torch.float32, device=dZ.device)
+    rc = _lib.load().c3cu_gemm_dw(_p(dZ), _p(X), _p(dW), M, N, K, lay, _stream(dZ.device))
+    _lib.check(rc, "c3cu_gemm_dw")
+    return dW
+
+
+def backward(dY: torch.Tensor, mask: torch.Tensor, X: torch.Tensor, W: torch.Tensor,
+             w_layout: str = "nk"):
+    """Captured backward of the region: returns (dX bf16, dW fp32, db fp32)."""
+    dZ, db = relu_mask_db(dY, mask)
+    dW = grad_weight(dZ, X, w_layout)
+    dX = grad_input(dZ, W, w_layout)
+    return dX, dW, db
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, a_mn: bool, b_mn: bool, epilogue: int,
+         out: torch.Tensor, bias: torch.Tensor | None = None, mask: torch.Tensor | None = None,
+         M: int | None = None, N: int | None = None, K: int | None = None):
+    """General tcgen05 GEMM out = epi(A B^T) (see c3cu_gemm_bf16 for the operand majors)."""
+    lda = A.stride(0)
+    ldb = B.stride(0)
+    rc = _lib.load().c3cu_gemm_bf16(_p(A), lda, int(a_mn), _p(B), ldb, int(b_mn), _p(out),
+                                    out.stride(0), epilogue, _p(bias), _p(mask),
+                                    0 if mask is None else mask.stride(0), M, N, K,
+                                    _stream(A.device))
+    _lib.check(rc, "c3cu_gemm_bf16")
+    return out

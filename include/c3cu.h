@@ -1,0 +1,144 @@
+/*
+ * c3cu.h — C ABI of the B200 (sm_100a) kernels behind the C3 fused hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, sizes and an explicit
+ * CUDA stream (`c3cu_stream_t` is a cudaStream_t; 0 = the legacy default stream), launches
+ * asynchronously and returns an int status: C3CU_OK (0) or a negative C3CU_ERR_* code.
+ * No C++ exception and no torch type crosses this boundary. The message of the last
+ * failure on the calling thread is available from c3cu_last_error().
+ *
+ * Layouts are row-major. "bf16" buffers hold IEEE bfloat16 (uint16_t bit patterns),
+ * "f32" buffers IEEE binary32. Pointers handed to the tensor-core entry points must be
+ * 16-byte aligned and their row strides multiples of 16 bytes (TMA rule); violations are
+ * reported as C3CU_ERR_ALIGN before anything is launched.
+ *
+ * Reference interface each entry point replaces (ShengFlow/C3, file:line):
+ *   c3cu_linear_bias_relu_fwd  <- the region kernel of "MatMul+Add+ReLU": MultiNodeKernelFunc
+ *                                 c3_kernel(inputs{X,B,b}, out, n, M, K, N, scratch)
+ *                                 (include/C3/C3KernelRegistry.h:80; built by
+ *                                 src/C3/MLIRKernelGen.cpp:783-1253, installed by
+ *                                 include/C3/C3HotPathManager.h:799-929)
+ *   c3cu_relu_mask_db          <- ReLU backward Mul(Gt(x,0),grad) (src/C3/C3BackwardCapture.cpp:501-528)
+ *                                 fused with Add backward SumReduce axis 0
+ *                                 (src/C3/C3BackwardCapture.cpp:618-644; src/C3/C3DialectLowering.cpp:382-465)
+ *   c3cu_gemm_dx / c3cu_gemm_dw <- MatMul backward grad@B^T and A^T@grad
+ *                                 (src/C3/C3BackwardCapture.cpp:681-723) executed through
+ *                                 C3KernelRegistry::tryExecuteBackward (src/C3/C3KernelRegistry.cpp:230-322)
+ *   c3cu_gemm_bf16             <- c3.matmul with transA/transB folding (src/C3/C3DialectLowering.cpp:467-610)
+ *   c3cu_ew_chain_cfg4 /
+ *   c3cu_ew_program            <- FusedNode elementwise loops (src/C3/MLIRKernelGen.cpp:394-768) and
+ *                                 LinalgFusedKernel (src/C3/LinalgFusedGen.cpp:141-378)
+ *   c3cu_sum_rows_f32          <- SumReduceOpLowering axis 0 (src/C3/C3DialectLowering.cpp:382-465)
+ */
+#ifndef C3CU_H_
+#define C3CU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* c3cu_stream_t;
+
+#define C3CU_OK 0
+#define C3CU_ERR_INVALID (-1)     /* null pointer, negative or unsupported size */
+#define C3CU_ERR_ALIGN (-2)       /* TMA alignment rule violated */
+#define C3CU_ERR_CUDA (-3)        /* CUDA runtime / driver error */
+#define C3CU_ERR_FAULT (-4)       /* a kernel recorded a fault (bounded wait gave up) */
+#define C3CU_ERR_UNSUPPORTED (-5) /* no sm_100 device current */
+#define C3CU_ERR_WORKSPACE (-6)   /* workspace missing or too small */
+
+#define C3CU_DTYPE_F32 0
+#define C3CU_DTYPE_BF16 1
+
+/* Weight layouts accepted by the Linear entry points. */
+#define C3CU_W_NK 0 /* W[N][K] (nn.Linear): Y = X * W^T */
+#define C3CU_W_KN 1 /* B[K][N] (the reference's MatMul rhs): Y = X * B */
+
+/* GEMM epilogues for c3cu_gemm_bf16. */
+#define C3CU_EPI_BIAS_RELU_MASK 0 /* out bf16 = max(acc+bias,0), mask bit = (acc+bias > 0) */
+#define C3CU_EPI_STORE_BF16 1
+#define C3CU_EPI_STORE_F32 2
+#define C3CU_EPI_BIAS_STORE_F32 3
+
+/* ------------------------------------------------------------------ library status */
+int c3cu_version(void);
+const char* c3cu_last_error(void);
+/* C3CU_OK when the current CUDA device is an sm_100 (B200-class) part. */
+int c3cu_device_check(void);
+/* Reads (and clears) the fault words the kernels write when a bounded wait gives up.
+ * Synchronises the device. *code = 0 when no kernel recorded a fault. */
+int c3cu_fault_status(uint32_t* code);
+
+/* ------------------------------------------------------------------ Linear+bias+ReLU
+ * Forward of the MatMul+Add+ReLU region: Y = max(X*W^T + b, 0) (C3CU_W_NK) or
+ * Y = max(X*B + b, 0) (C3CU_W_KN); bf16 inputs, fp32 accumulation, bf16 output.
+ * mask: [M][ceil(N/32)] uint32, bit j of word w = (pre-activation[m][32w+j] > 0). */
+int c3cu_linear_bias_relu_fwd(const void* X, const void* W, const float* bias, void* Y,
+                              uint32_t* mask, int64_t M, int64_t N, int64_t K, int w_layout,
+                              c3cu_stream_t stream);
+
+/* Backward pre-pass: dZ = dY * mask (bf16, exact) and db[n] = sum_m dZ[m][n] (fp32).
+ * Needs a device workspace of c3cu_relu_mask_db_workspace(M, N) bytes. */
+size_t c3cu_relu_mask_db_workspace(int64_t M, int64_t N);
+int c3cu_relu_mask_db(const void* dY, const uint32_t* mask, void* dZ, float* db, int64_t M,
+                      int64_t N, void* workspace, size_t workspace_bytes, c3cu_stream_t stream);
+
+/* dX = dZ * W (C3CU_W_NK, W[N][K]) or dZ * B^T (C3CU_W_KN, B[K][N]); bf16 out [M][K]. */
+int c3cu_gemm_dx(const void* dZ, const void* W, void* dX, int64_t M, int64_t N, int64_t K,
+                 int w_layout, c3cu_stream_t stream);
+
+/* dW = dZ^T * X as fp32 [N][K] (C3CU_W_NK) or dB = X^T * dZ as fp32 [K][N] (C3CU_W_KN). */
+int c3cu_gemm_dw(const void* dZ, const void* X, float* dW, int64_t M, int64_t N, int64_t K,
+                 int w_layout, c3cu_stream_t stream);
+
+/* General tensor-core GEMM: out[M][N] = epi(A * B^T) with
+ *   A: a_mn == 0 -> stored [M][lda] (K contiguous); a_mn == 1 -> stored [K][lda] (M contiguous)
+ *   B: b_mn == 0 -> stored [N][ldb] (K contiguous); b_mn == 1 -> stored [K][ldb] (N contiguous)
+ * out row stride ldo (elements), mask row stride ldm (words). */
+int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                   void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,
+                   int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream);
+
+/* ------------------------------------------------------------------ elementwise chains
+ * The chain relu((A + B) * C - A) / (1 + exp(-B)) over n fp32 elements, one pass. */
+int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* out, int64_t n,
+                       c3cu_stream_t stream);
+
+/* General single-pass chain. `code` holds n_instr instructions of 4 bytes
+ * {opcode, dst, src0, src1} over 16 fp32 registers; registers 0..n_inputs-1 are loaded
+ * from inputs[i][idx % numels[i]] (numels[i] == n: no broadcast), and register `out_reg`
+ * is stored to out[idx]. Opcodes: see C3CU_EW_* below. */
+#define C3CU_EW_MAX_INPUTS 8
+#define C3CU_EW_MAX_INSTR 32
+#define C3CU_EW_ADD 1
+#define C3CU_EW_SUB 2
+#define C3CU_EW_MUL 3
+#define C3CU_EW_DIV 4        /* plain IEEE division */
+#define C3CU_EW_DIV_NANZ 5   /* division returning NaN when the divisor is 0 */
+#define C3CU_EW_NEG 6
+#define C3CU_EW_RELU 7       /* maxnum(x, 0) */
+#define C3CU_EW_EXP 8
+#define C3CU_EW_LOG 9
+#define C3CU_EW_SIGMOID 10   /* 1 / (1 + exp(-x)) */
+#define C3CU_EW_TANH 11      /* tanh(x) */
+#define C3CU_EW_TANH_EXP 12  /* (exp(x) - exp(-x)) / (exp(x) + exp(-x)) */
+#define C3CU_EW_GT 13        /* src0 > src1 ? 1 : 0 (ordered: NaN -> 0) */
+#define C3CU_EW_CONST 14     /* dst = constant table[src0] */
+#define C3CU_EW_MOV 15
+int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,
+                    const uint8_t* code, int n_instr, const float* constants, int n_constants,
+                    int out_reg, float* out, int64_t n, c3cu_stream_t stream);
+
+/* db[n] = sum over rows of a fp32 matrix [M][N] (axis 0), deterministic order. */
+size_t c3cu_sum_rows_f32_workspace(int64_t M, int64_t N);
+int c3cu_sum_rows_f32(const float* in, float* out, int64_t M, int64_t N, void* workspace,
+                      size_t workspace_bytes, c3cu_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* C3CU_H_ */

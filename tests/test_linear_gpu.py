@@ -1,0 +1,202 @@
+"""Parity of the tcgen05 Linear+bias+ReLU forward and its captured backward against the
+oracle (the reference's fp32 loop arithmetic restated in C), on the same bf16-rounded inputs.
+
+Tolerances: bf16 tensor-core outputs <= 2e-2 relative (normwise and per element with an
+rms floor); dZ (mask apply) bit-exact; ReLU mask bit-exact against the kernel's own
+pre-activation (mask == (Y > 0)), and against the oracle's fp32 pre-activation except for
+sign flips at |z| below the accumulation-order error."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from c3_b200 import linear
+from tests.helpers import (TOL_BF16, assert_bf16_close, f32, pack_mask, randn, rel_err,
+                           unpack_mask)
+
+pytestmark = pytest.mark.gpu
+
+# (M, N, K): tile-aligned, ragged in every dimension, tiny, the cfg1 layer shapes.
+SHAPES = [
+    (128, 256, 64),
+    (256, 512, 256),
+    (200, 264, 136),
+    (1, 8, 8),
+    (130, 40, 24),
+    (300, 520, 1000),
+    (128, 256, 784),
+    (128, 128, 256),
+    (517, 1032, 776),
+]
+
+
+def _fwd_inputs(M, N, K, seed, dev):
+    X = randn((M, K), 1.0, seed)
+    W = randn((N, K), 1.0 / np.sqrt(K), seed + 1)
+    b = randn((N,), 0.1, seed + 2, torch.float32)
+    return X.to(dev), W.to(dev), b.to(dev)
+
+
+def _check_mask(mask_words, Y, z_ref, N):
+    bits = unpack_mask(mask_words, N)
+    # exact against the kernel's own pre-activation: bit set <=> output > 0
+    assert np.array_equal(bits, Y > 0), "mask disagrees with the kernel's own ReLU output"
+    flips = bits != (z_ref > 0)
+    if flips.any():
+        scale = float(np.sqrt(np.mean(z_ref.astype(np.float64) ** 2)))
+        worst = float(np.abs(z_ref[flips]).max())
+        assert worst <= 1e-3 * scale, f"{int(flips.sum())} mask flips, max |z_ref| {worst:.3e}"
+    return int(flips.sum())
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("w_layout", ["nk", "kn"])
+def test_forward_parity(cuda_device, M, N, K, w_layout):
+    X, W, b = _fwd_inputs(M, N, K, 100 + M + N + K, cuda_device)
+    Wl = W if w_layout == "nk" else W.t().contiguous()
+    Y, mask = linear.forward(X, Wl, b, w_layout)
+    torch.cuda.synchronize()
+    out_ref, z_ref = oracle.region_fwd(f32(X), f32(W), f32(b), transB=True)
+    assert_bf16_close(f32(Y), out_ref, f"Y[{M},{N},{K}]")
+    _check_mask(mask.cpu().numpy().view(np.uint32), f32(Y), z_ref, N)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("w_layout", ["nk", "kn"])
+def test_backward_parity(cuda_device, M, N, K, w_layout):
+    seed = 700 + M + N + K
+    X = randn((M, K), 1.0, seed).to(cuda_device)
+    W = randn((N, K), 1.0 / np.sqrt(K), seed + 1).to(cuda_device)
+    dY = randn((M, N), 1e-3, seed + 2).to(cuda_device)
+    rng = np.random.default_rng(seed)
+    bits = rng.random((M, N)) < 0.5
+    mask_np = pack_mask(bits)
+    mask = torch.from_numpy(mask_np.view(np.int32)).to(cuda_device)
+    Wl = W if w_layout == "nk" else W.t().contiguous()
+
+    dZ, db = linear.relu_mask_db(dY, mask)
+    dX = linear.grad_input(dZ, Wl, w_layout)
+    dW = linear.grad_weight(dZ, X, w_layout)
+    torch.cuda.synchronize()
+
+    dZ_ref = oracle.relu_bwd_mask(f32(dY), mask_np)
+    # dZ is a masked copy of bf16 values: bit-exact, signed zeros included
+    assert np.array_equal(f32(dZ).view(np.uint32), dZ_ref.view(np.uint32))
+    db_ref = oracle.sum_reduce(dZ_ref, axis=0)
+    bound = 1e-5 * np.abs(dZ_ref).sum(axis=0) + 1e-12
+    assert (np.abs(f32(db) - db_ref) <= bound).all(), "db outside 1e-5 * sum|dZ|"
+
+    dX_ref = oracle.matmul(dZ_ref, f32(W))  # dX = dZ W, W [N, K]
+    assert_bf16_close(f32(dX), dX_ref, f"dX[{M},{N},{K}]")
+    dW_ref = oracle.matmul(dZ_ref, f32(X), transA=True)  # dW = dZ^T X, [N, K]
+    got = f32(dW) if w_layout == "nk" else f32(dW).T
+    assert_bf16_close(got, dW_ref, f"dW[{M},{N},{K}]")
+    # fp32 output of exact bf16 products: only the summation order differs
+    assert rel_err(got, dW_ref) < 1e-4
+
+
+def test_forward_mask_from_forward_feeds_backward(cuda_device):
+    """End to end: the forward's own mask drives the backward (as the captured graph does)."""
+    M, N, K = 384, 768, 512
+    X, W, b = _fwd_inputs(M, N, K, 5, cuda_device)
+    Y, mask = linear.forward(X, W, b)
+    dY = randn((M, N), 1e-3, 6).to(cuda_device)
+    dX, dW, db = linear.backward(dY, mask, X, W)
+    torch.cuda.synchronize()
+    _, z_ref = oracle.region_fwd(f32(X), f32(W), f32(b), transB=True)
+    dZ_ref = oracle.relu_bwd(f32(dY), z_ref)
+    bits = unpack_mask(mask.cpu().numpy().view(np.uint32), N)
+    agree = bits == (z_ref > 0)
+    # where the kernel's mask agrees with the oracle's sign, the gradients must match
+    dZ_k = f32(dY) * bits
+    assert np.array_equal(dZ_k[agree], dZ_ref[agree])
+    assert_bf16_close(f32(dX), oracle.matmul(dZ_k, f32(W)), "dX e2e")
+    assert_bf16_close(f32(dW), oracle.matmul(dZ_k, f32(X), transA=True), "dW e2e")
+    assert np.abs(f32(db) - dZ_k.sum(axis=0, dtype=np.float64)).max() <= 1e-5 * np.abs(dZ_k).sum(0).max() + 1e-9
+
+
+def test_general_gemm_epilogues(cuda_device):
+    M, N, K = 200, 300, 160
+    A = randn((M, K), 1.0, 11).to(cuda_device)
+    B = randn((N, K), 0.1, 12).to(cuda_device)
+    bias = randn((N,), 0.5, 13, torch.float32).to(cuda_device)
+    ref = f32(A) @ f32(B).T
+    out = torch.empty((M, N), dtype=torch.float32, device=cuda_device)
+    linear.gemm(A, B, False, False, 3, out, bias=bias, M=M, N=N, K=K)
+    out2 = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_device)
+    linear.gemm(A, B, False, False, 1, out2, M=M, N=N, K=K)
+    torch.cuda.synchronize()
+    assert rel_err(f32(out), ref + f32(bias)) < 1e-4
+    assert_bf16_close(f32(out2), ref, "store_bf16")
+
+
+def test_rejects_misaligned_and_bad_shapes(cuda_device):
+    from c3_b200 import C3CUError
+    X = torch.zeros((16, 12), dtype=torch.bfloat16, device=cuda_device)  # 24-byte rows
+    W = torch.zeros((8, 12), dtype=torch.bfloat16, device=cuda_device)
+    b = torch.zeros(8, dtype=torch.float32, device=cuda_device)
+    with pytest.raises(C3CUError) as e:
+        linear.forward(X, W, b)
+    assert e.value.code == -2  # C3CU_ERR_ALIGN
+    with pytest.raises(C3CUError):
+        linear.forward(X[:, :8].contiguous(), W, b[:4].contiguous())
+
+
+def test_empty_rows(cuda_device):
+    X = torch.zeros((0, 64), dtype=torch.bfloat16, device=cuda_device)
+    W = torch.zeros((32, 64), dtype=torch.bfloat16, device=cuda_device)
+    b = torch.zeros(32, dtype=torch.float32, device=cuda_device)
+    Y, mask = linear.forward(X, W, b)
+    assert Y.shape == (0, 32) and mask.shape == (0, 1)
+
+
+@pytest.mark.parametrize("M", [8192])
+def test_cfg2_forward_full_size_sampled(cuda_device, M):
+    """BASELINE cfg2 at full size: X[8192,4096] N(0,1), W[4096,4096] N(0,0.02), b N(0,0.01).
+    Rows are checked against the oracle on a random sample (the oracle is O(N K) per row)."""
+    N = K = 4096
+    g = torch.Generator(device=cuda_device).manual_seed(2)
+    X = torch.randn((M, K), generator=g, device=cuda_device).to(torch.bfloat16)
+    W = (torch.randn((N, K), generator=g, device=cuda_device) * 0.02).to(torch.bfloat16)
+    b = torch.randn((N,), generator=g, device=cuda_device) * 0.01
+    Y, mask = linear.forward(X, W, b)
+    torch.cuda.synchronize()
+    rows = np.sort(np.random.default_rng(0).choice(M, 24, replace=False))
+    rows = np.concatenate([[0, M - 1], rows])
+    Xs = f32(X[torch.as_tensor(rows, device=cuda_device)])
+    out_ref, z_ref = oracle.region_fwd(Xs, f32(W), f32(b), transB=True, threads=8)
+    Ys = f32(Y[torch.as_tensor(rows, device=cuda_device)])
+    assert_bf16_close(Ys, out_ref, "cfg2 Y (sampled rows)")
+    _check_mask(mask[torch.as_tensor(rows, device=cuda_device)].cpu().numpy().view(np.uint32), Ys, z_ref, N)
+    # size-independent property over the whole output: mask == (Y > 0) everywhere
+    bits_all = unpack_mask(mask.cpu().numpy().view(np.uint32), N)
+    assert np.array_equal(bits_all, f32(Y) > 0)
+
+
+def test_cfg3_backward_full_size_sampled(cuda_device):
+    """BASELINE cfg3 at full size on one GPU: dY[16384,4096] N(0,1e-3), X N(0,1), W N(0,0.02),
+    mask from the forward. dX rows and dW rows are checked on random samples; db in full."""
+    M, N, K = 16384, 4096, 4096
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    X = torch.randn((M, K), generator=g, device=cuda_device).to(torch.bfloat16)
+    W = (torch.randn((N, K), generator=g, device=cuda_device) * 0.02).to(torch.bfloat16)
+    b = torch.randn((N,), generator=g, device=cuda_device) * 0.01
+    dY = (torch.randn((M, N), generator=g, device=cuda_device) * 1e-3).to(torch.bfloat16)
+    _, mask = linear.forward(X, W, b)
+    dZ, db = linear.relu_mask_db(dY, mask)
+    dX = linear.grad_input(dZ, W)
+    dW = linear.grad_weight(dZ, X)
+    torch.cuda.synchronize()
+    # dZ: exact masked copy (checked on the device, whole tensor)
+    bits = torch.from_numpy(unpack_mask(mask.cpu().numpy().view(np.uint32), N)).to(cuda_device)
+    assert torch.equal(dZ.view(torch.int16), (dY.float() * bits.float()).to(torch.bfloat16).view(torch.int16))
+    dZf = f32(dZ)
+    db_ref = dZf.sum(axis=0, dtype=np.float64)
+    assert (np.abs(f32(db) - db_ref) <= 1e-5 * np.abs(dZf).sum(0) + 1e-12).all()
+    rng = np.random.default_rng(1)
+    rows = np.sort(rng.choice(M, 16, replace=False))
+    dX_ref = oracle.matmul(dZf[rows], f32(W), threads=8)
+    assert_bf16_close(f32(dX)[rows], dX_ref, "cfg3 dX (sampled rows)")
+    wrows = np.sort(rng.choice(N, 8, replace=False))
+    dW_ref = oracle.matmul(np.ascontiguousarray(dZf[:, wrows]), f32(X), transA=True, threads=8)
+    assert_bf16_close(f32(dW)[wrows], dW_ref, "cfg3 dW (sampled rows)")
