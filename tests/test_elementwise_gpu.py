@@ -84,7 +84,12 @@ def test_program_parity(cuda_device, name, n):
     b = torch.rand(n, generator=g) * 4 - 2
     c = torch.rand(max(1, n // 1), generator=g) * 4 - 2
     if name == "mixed":
-        c[::7] = 0.0  # divisor zeros exercise the NaN-on-zero division
+        # The exp-form tanh cancels catastrophically near 0 and a small divisor amplifies
+        # that: keep |a| >= 0.5 and |c| >= 0.5 so a 1-ulp expf difference between libms
+        # stays within tolerance; exact zeros in c exercise the NaN-on-zero division.
+        a = torch.sign(a) * (a.abs() + 0.5)
+        c = torch.sign(c) * (c.abs() + 0.5)
+        c[::7] = 0.0
     ins = [a, b, c]
     out = ew.program([t.to(cuda_device) for t in ins], code, consts, out_reg, n)
     torch.cuda.synchronize()
