@@ -293,6 +293,10 @@ def run_c3(args):
     gemm_flops = 3 * 2.0 * M * N * K
     peak_burst, peak_sust, hbm, peak_kind = _peaks()
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    # A timed region of seconds runs under the power cap (sustained figure); a shorter one
+    # is compared with the burst figure.
+    long_region = elapsed_ms > 2000.0
+    peak = peak_sust if long_region else peak_burst
     traffic = _traffic()
 
     # ------------------------------------------------------------------ e2e (host buffers)
@@ -310,12 +314,15 @@ def run_c3(args):
                        "l2": "inputs larger than L2 (X, dY 128 MiB each at N=1)",
                        "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
                                + (", NCCL all-reduce [dW|db] overlapped with dX" if world > 1 else "")},
-            "frac_of_peak": value / world / peak_sust,
+            "frac_of_peak": value / world / peak,
             "kernel_ms": ktime,
             "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",
-                         "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
-                         "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} sustained",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} {'sustained' if long_region else 'burst'}",
                          "frac_of_burst": achieved / peak_burst,
+                         "frac_of_sustained": achieved / peak_sust,
+                         "frac_of_spec_2250": achieved / 2250.0,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None},
             "gpu_launches": 4 * args.steps,
             "clocks": sampler.record(),
@@ -398,8 +405,8 @@ def run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["c3", "reference"], default="c3")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

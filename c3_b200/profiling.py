@@ -1,0 +1,92 @@
+"""Runs one hot-path kernel repeatedly on cuda:0, for timing and for ncu captures.
+
+    python -m c3_b200.profiling <case> [--iters N] [--m M] [--n N] [--k K] [--elems E]
+
+cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step
+Prints the CUDA-event time per launch and the algorithmic rate (TFLOP/s or GB/s)."""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import elementwise, linear
+
+
+def _case(args, dev):
+    g = torch.Generator(device=dev).manual_seed(0)
+    M, N, K = args.m, args.n, args.k
+    if args.case.startswith("gemm") or args.case in ("prepass", "step"):
+        X = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        W = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        b = torch.randn((N,), generator=g, device=dev) * 0.01
+        dY = (torch.randn((M, N), generator=g, device=dev) * 1e-3).to(torch.bfloat16)
+        Y, mask = linear.forward(X, W, b)
+        dZ, db = linear.relu_mask_db(dY, mask)
+        dW = torch.empty((N, K), dtype=torch.float32, device=dev)
+        dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+        fl = 2.0 * M * N * K
+        if args.case == "gemm-fwd":
+            return (lambda: linear.forward(X, W, b, "nk", Y, mask)), fl, "TFLOP/s"
+        if args.case == "gemm-dw":
+            return (lambda: linear.grad_weight(dZ, X, "nk", dW)), fl, "TFLOP/s"
+        if args.case == "gemm-dx":
+            return (lambda: linear.grad_input(dZ, W, "nk", dX)), fl, "TFLOP/s"
+        if args.case == "prepass":
+            nbytes = M * N * 2 * 2 + M * ((N + 31) // 32) * 4 + N * 4
+            return (lambda: linear.relu_mask_db(dY, mask, dZ, db)), nbytes, "GB/s"
+
+        def step():
+            linear.forward(X, W, b, "nk", Y, mask)
+            linear.relu_mask_db(dY, mask, dZ, db)
+            linear.grad_weight(dZ, X, "nk", dW)
+            linear.grad_input(dZ, W, "nk", dX)
+        return step, 3 * fl, "TFLOP/s"
+    if args.case == "ew-cfg4":
+        n = args.elems
+        A = torch.rand(n, generator=g, device=dev) * 8 - 4
+        B = torch.rand(n, generator=g, device=dev) * 16 - 8
+        C = torch.rand(n, generator=g, device=dev) * 8 - 4
+        out = torch.empty_like(A)
+        return (lambda: elementwise.chain_cfg4(A, B, C, out)), 16.0 * n, "GB/s"
+    if args.case == "sum-rows":
+        x = torch.randn((M, N), generator=g, device=dev)
+        out = torch.empty(N, device=dev)
+        return (lambda: elementwise.sum_rows(x, out)), 4.0 * M * N, "GB/s"
+    raise SystemExit(f"unknown case {args.case}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--elems", type=int, default=1 << 28)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    fn, work, unit = _case(args, dev)
+    fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    from . import fault_status
+    fault_status()
+    best, avg = min(times), sum(times) / len(times)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    print(json.dumps({"case": args.case, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
+                      "ms_avg": avg, "ms_best": best, "rate_avg": work / (avg * 1e-3) / scale,
+                      "rate_best": work / (best * 1e-3) / scale, "unit": unit}))
+
+
+if __name__ == "__main__":
+    main()
