@@ -48,6 +48,10 @@ _SIGNATURES = {
     "c3cu_ew_program": ([_vp, _vp, _i, _vp, _i, _vp, _i, _i, _vp, _i64, _vp], _i),
     "c3cu_sum_rows_f32_workspace": ([_i64, _i64], _sz),
     "c3cu_sum_rows_f32": ([_vp, _vp, _i64, _i64, _vp, _sz, _vp], _i),
+    "c3cu_matmul_f32": ([_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp, _i64, _i, _vp], _i),
+    "c3cu_region_fwd_f32": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i, _vp], _i),
+    "c3cu_sum_rows_f32_exact": ([_vp, _vp, _i64, _i64, _vp], _i),
+    "c3cu_convert": ([_vp, _i, _vp, _i, _i64, _vp], _i),
 }
 
 

@@ -314,6 +314,20 @@ __global__ void __launch_bounds__(256) program_kernel(const Program prog, float*
   }
 }
 
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ in,
+                                                          __nv_bfloat16* __restrict__ out, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = __float2bfloat16_rn(in[i]);
+}
+
+__global__ void __launch_bounds__(256) bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ in,
+                                                          float* __restrict__ out, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = __bfloat162float(in[i]);
+}
+
 int grid_for(int64_t work_items, int threads) {
   const int64_t sms = sm_count() > 0 ? sm_count() : 148;
   const int64_t want = (work_items + threads - 1) / threads;
@@ -366,6 +380,34 @@ int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* ou
   c3cu::ew::chain_cfg4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(A, B, C, out, n,
                                                                                    vec_ok);
   return c3cu::cuda_status(cudaGetLastError(), "ew_chain_cfg4: launch");
+}
+
+int c3cu_convert(const void* in, int in_dtype, void* out, int out_dtype, int64_t n,
+                 c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (n < 0 || (n > 0 && (!in || !out))) {
+    c3cu::set_error("convert: bad arguments");
+    return C3CU_ERR_INVALID;
+  }
+  if (n == 0) return C3CU_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = c3cu::ew::grid_for(n, 256);
+  if (in_dtype == out_dtype) {
+    const size_t bytes = static_cast<size_t>(n) * (in_dtype == C3CU_DTYPE_BF16 ? 2u : 4u);
+    return c3cu::cuda_status(cudaMemcpyAsync(out, in, bytes, cudaMemcpyDeviceToDevice, st), "convert: copy");
+  }
+  if (in_dtype == C3CU_DTYPE_F32 && out_dtype == C3CU_DTYPE_BF16)
+    c3cu::ew::f32_to_bf16_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(in),
+                                                       static_cast<__nv_bfloat16*>(out), n);
+  else if (in_dtype == C3CU_DTYPE_BF16 && out_dtype == C3CU_DTYPE_F32)
+    c3cu::ew::bf16_to_f32_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(in),
+                                                       static_cast<float*>(out), n);
+  else {
+    c3cu::set_error("convert: unsupported dtypes %d -> %d", in_dtype, out_dtype);
+    return C3CU_ERR_INVALID;
+  }
+  return c3cu::cuda_status(cudaGetLastError(), "convert: launch");
 }
 
 int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,

@@ -1,0 +1,209 @@
+// Bit-exact fp32 kernels (CUDA cores) for the reference's fp32 arithmetic:
+//   * c3cu_matmul_f32      — c3.matmul: acc = bias-or-0; for k ascending: acc = acc + a*b
+//                            (separate round-to-nearest multiply and add, no FMA), then act
+//                            (src/C3/C3DialectLowering.cpp:467-610)
+//   * c3cu_region_fwd_f32  — MatMul+Add+ReLU region: T (as above, from 0), then
+//                            out = maxnum(T + b[idx % numel(b)], 0), optional pre-activation
+//                            and bit mask (src/C3/MLIRKernelGen.cpp:610-768)
+//   * c3cu_sum_rows_f32_exact — SumReduce axis 0 in the reference's row order
+//                            (src/C3/C3DialectLowering.cpp:382-465)
+// Register tiling changes which thread computes an element, never the order of the k
+// reduction of that element, so these kernels reproduce the reference's results bit for
+// bit (expf/tanhf of the sigmoid/tanh activations aside, which use CUDA's libm).
+#include "common.cuh"
+#include "host_util.h"
+
+namespace c3cu {
+namespace exact {
+
+constexpr int TM = 64, TN = 64, TK = 16;  // block tile; 256 threads, 4x4 outputs each
+
+template <bool TA, bool TB>
+__device__ __forceinline__ float load_a(const float* A, int i, int k, int M, int K) {
+  if (i >= M || k >= K) return 0.f;
+  return TA ? A[(int64_t)k * M + i] : A[(int64_t)i * K + k];
+}
+
+template <bool TA, bool TB>
+__device__ __forceinline__ float load_b(const float* B, int k, int j, int K, int N) {
+  if (j >= N || k >= K) return 0.f;
+  return TB ? B[(int64_t)j * K + k] : B[(int64_t)k * N + j];
+}
+
+// MODE 0: out = act(bias_init + sum)     (plain c3.matmul)
+// MODE 1: s = sum + b[idx % bn]; out = maxnum(s, 0); z = s; mask bits (region forward)
+template <bool TA, bool TB, int MODE>
+__global__ void __launch_bounds__(256)
+    sgemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                       float* __restrict__ out, float* __restrict__ z, uint32_t* __restrict__ mask,
+                       const float* __restrict__ bias, int64_t bias_numel, int M, int K, int N,
+                       int act) {
+  __shared__ float As[TK][TM + 4];
+  __shared__ float Bs[TK][TN + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float init = 0.f;
+      if (MODE == 0 && bias != nullptr) {
+        const int col = n0 + tx * 4 + j;
+        init = (col < N) ? bias[bias_numel == 1 ? 0 : col] : 0.f;
+      }
+      acc[i][j] = init;
+    }
+  for (int k0 = 0; k0 < K; k0 += TK) {
+    // 256 threads load 64x16 of A and 16x64 of B (4 elements each)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int e = threadIdx.x + r * 256;
+      const int am = e / TK, ak = e % TK;  // A tile: [TM][TK]
+      As[ak][am] = load_a<TA, TB>(A, m0 + am, k0 + ak, M, K);
+      const int bk = e / TN, bn = e % TN;  // B tile: [TK][TN]
+      Bs[bk][bn] = load_b<TA, TB>(B, k0 + bk, n0 + bn, K, N);
+    }
+    __syncthreads();
+    const int kmax = min(TK, K - k0);
+    for (int kk = 0; kk < kmax; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = m0 + ty * 4 + i;
+    if (row >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = n0 + tx * 4 + j;
+      if (col >= N) continue;
+      const int64_t idx = (int64_t)row * N + col;
+      const float t = acc[i][j];
+      if (MODE == 0) {
+        float v = t;
+        if (act == 1) {
+          v = fmaxf(t, 0.f);
+        } else if (act == 2) {
+          v = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-t)));
+        } else if (act == 3) {
+          v = tanhf(t);
+        }
+        out[idx] = v;
+      } else {
+        const float s = __fadd_rn(t, bias[idx % bias_numel]);
+        out[idx] = fmaxf(s, 0.f);
+        if (z) z[idx] = s;
+        if (mask && s > 0.f) atomicOr(mask + (int64_t)row * ((N + 31) / 32) + (col >> 5), 1u << (col & 31));
+      }
+    }
+  }
+}
+
+// One thread per column, rows ascending: the reference's accumulation order exactly.
+__global__ void __launch_bounds__(256)
+    sum_rows_exact_kernel(const float* __restrict__ in, float* __restrict__ out, int M, int N) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= N) return;
+  float s = 0.f;
+  for (int i = 0; i < M; ++i) s = __fadd_rn(s, in[(int64_t)i * N + j]);
+  out[j] = s;
+}
+
+template <bool TA, bool TB, int MODE>
+int launch(const float* A, const float* B, float* out, float* z, uint32_t* mask, const float* bias,
+           int64_t bias_numel, int64_t M, int64_t K, int64_t N, int act, cudaStream_t st) {
+  dim3 grid(static_cast<unsigned>((N + TN - 1) / TN), static_cast<unsigned>((M + TM - 1) / TM));
+  if (grid.y > 65535) {
+    set_error("exact matmul: M=%lld too large", (long long)M);
+    return C3CU_ERR_INVALID;
+  }
+  sgemm_exact_kernel<TA, TB, MODE><<<grid, 256, 0, st>>>(A, B, out, z, mask, bias, bias_numel,
+                                                         static_cast<int>(M), static_cast<int>(K),
+                                                         static_cast<int>(N), act);
+  return cuda_status(cudaGetLastError(), "exact matmul: launch");
+}
+
+template <int MODE>
+int dispatch(int ta, int tb, const float* A, const float* B, float* out, float* z, uint32_t* mask,
+             const float* bias, int64_t bn, int64_t M, int64_t K, int64_t N, int act,
+             cudaStream_t st) {
+  if (!ta && !tb) return launch<false, false, MODE>(A, B, out, z, mask, bias, bn, M, K, N, act, st);
+  if (!ta && tb) return launch<false, true, MODE>(A, B, out, z, mask, bias, bn, M, K, N, act, st);
+  if (ta && !tb) return launch<true, false, MODE>(A, B, out, z, mask, bias, bn, M, K, N, act, st);
+  return launch<true, true, MODE>(A, B, out, z, mask, bias, bn, M, K, N, act, st);
+}
+
+int check_sizes(int64_t M, int64_t K, int64_t N) {
+  if (M < 0 || K < 0 || N < 0 || M > INT32_MAX || K > INT32_MAX || N > INT32_MAX) {
+    set_error("exact matmul: sizes out of range");
+    return C3CU_ERR_INVALID;
+  }
+  return require_sm100();
+}
+
+}  // namespace exact
+}  // namespace c3cu
+
+extern "C" {
+
+int c3cu_matmul_f32(const float* A, const float* B, float* out, int64_t M, int64_t K, int64_t N,
+                    int transA, int transB, const float* bias, int64_t bias_numel, int act,
+                    c3cu_stream_t stream) {
+  int rc = c3cu::exact::check_sizes(M, K, N);
+  if (rc != C3CU_OK) return rc;
+  if (M == 0 || N == 0) return C3CU_OK;
+  if (!A || !B || !out || (bias && bias_numel <= 0) || act < 0 || act > 3) {
+    c3cu::set_error("matmul_f32: bad arguments");
+    return C3CU_ERR_INVALID;
+  }
+  return c3cu::exact::dispatch<0>(transA != 0, transB != 0, A, B, out, nullptr, nullptr, bias,
+                                  bias_numel, M, K, N, act, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_region_fwd_f32(const float* X, const float* B, const float* bias, int64_t bias_numel,
+                        float* out, float* z, uint32_t* mask, int64_t M, int64_t K, int64_t N,
+                        int transB, c3cu_stream_t stream) {
+  int rc = c3cu::exact::check_sizes(M, K, N);
+  if (rc != C3CU_OK) return rc;
+  if (M == 0 || N == 0) return C3CU_OK;
+  if (!X || !B || !out || !bias || bias_numel <= 0) {
+    c3cu::set_error("region_fwd_f32: bad arguments");
+    return C3CU_ERR_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mask) {
+    rc = c3cu::cuda_status(
+        cudaMemsetAsync(mask, 0, static_cast<size_t>(M) * static_cast<size_t>((N + 31) / 32) * 4u, st),
+        "region_fwd_f32: clear mask");
+    if (rc != C3CU_OK) return rc;
+  }
+  return c3cu::exact::dispatch<1>(0, transB != 0, X, B, out, z, mask, bias, bias_numel, M, K, N, 0,
+                                  st);
+}
+
+int c3cu_sum_rows_f32_exact(const float* in, float* out, int64_t M, int64_t N,
+                            c3cu_stream_t stream) {
+  int rc = c3cu::exact::check_sizes(M, 1, N);
+  if (rc != C3CU_OK) return rc;
+  if (N == 0) return C3CU_OK;
+  if (!out || (M > 0 && !in)) {
+    c3cu::set_error("sum_rows_f32_exact: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  const int grid = static_cast<int>((N + 255) / 256);
+  c3cu::exact::sum_rows_exact_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      in, out, static_cast<int>(M), static_cast<int>(N));
+  return c3cu::cuda_status(cudaGetLastError(), "sum_rows_f32_exact: launch");
+}
+
+}  // extern "C"

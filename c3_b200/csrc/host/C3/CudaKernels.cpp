@@ -1,0 +1,451 @@
+#include "C3/CudaKernels.h"
+
+#include <algorithm>
+#include <map>
+#include <sstream>
+#include <stdexcept>
+
+#include "C3/CudaRuntime.h"
+#include "c3cu.h"
+
+namespace ct {
+namespace c3 {
+
+namespace {
+
+using cuda::checkAbi;
+
+c3cu_stream_t stream() { return static_cast<c3cu_stream_t>(cuda::currentStream()); }
+
+std::string shapeStr(const std::vector<size_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? "," : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+void expectShape(const Tensor& t, const std::vector<size_t>& shape, const char* what) {
+  if (t.shape() != shape)
+    throw std::runtime_error(std::string(what) + ": expected shape " + shapeStr(shape) + ", got " +
+                             shapeStr(t.shape()));
+}
+
+Tensor newDevice(const std::vector<size_t>& shape, DType dt) {
+  return Tensor(ShapeTag{}, shape, dt, DeviceType::kCUDA);
+}
+
+int abiDtype(DType d) { return d == DType::kBF16 ? C3CU_DTYPE_BF16 : C3CU_DTYPE_F32; }
+
+Tensor convert(const Tensor& t, DType to) {
+  if (t.dtype() == to) return t;
+  if (t.dtype() == DType::kInt32 || to == DType::kInt32)
+    throw std::runtime_error("convert: int32 tensors are not converted");
+  Tensor out = newDevice(t.shape(), to);
+  checkAbi(c3cu_convert(t.data(), abiDtype(t.dtype()), out.data(), abiDtype(to),
+                        static_cast<int64_t>(t.numel()), stream()),
+           "convert");
+  return out;
+}
+
+// Runs a register-machine program over fp32 device inputs.
+Tensor runProgram(const std::vector<Tensor>& ins, const std::vector<uint8_t>& code,
+                  const std::vector<float>& consts, int out_reg, const std::vector<size_t>& out_shape) {
+  std::vector<const float*> ptrs;
+  std::vector<int64_t> numels;
+  std::vector<Tensor> keep;
+  for (const auto& t : ins) {
+    Tensor f = convert(t, DType::kFloat);
+    keep.push_back(f);
+    ptrs.push_back(static_cast<const float*>(f.data()));
+    numels.push_back(static_cast<int64_t>(f.numel()));
+  }
+  Tensor out = newDevice(out_shape, DType::kFloat);
+  checkAbi(c3cu_ew_program(ptrs.data(), numels.data(), static_cast<int>(ptrs.size()), code.data(),
+                           static_cast<int>(code.size() / 4), consts.data(),
+                           static_cast<int>(consts.size()), out_reg, static_cast<float*>(out.data()),
+                           static_cast<int64_t>(out.numel()), stream()),
+           "ew_program");
+  return out;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------- staging
+std::vector<Tensor> CudaKernelBase::execute(const std::vector<Tensor>& inputs) {
+  if (inputs.size() != expectedInputs())
+    throw std::runtime_error(describe() + ": expected " + std::to_string(expectedInputs()) +
+                             " inputs, got " + std::to_string(inputs.size()));
+  bool host_io = false;
+  std::vector<Tensor> dev;
+  dev.reserve(inputs.size());
+  for (const auto& t : inputs) {
+    if (!t.defined()) throw std::runtime_error(describe() + ": undefined input");
+    if (t.device() == DeviceType::kCUDA) {
+      dev.push_back(t);
+    } else if (t.device() == DeviceType::kCPU) {
+      host_io = true;
+      dev.push_back(t.to(DeviceType::kCUDA));
+    } else {
+      throw std::runtime_error(describe() + ": inputs must be host or CUDA tensors");
+    }
+  }
+  std::vector<Tensor> outs = run(dev);
+  if (host_io) {
+    for (auto& o : outs) o = o.to(DeviceType::kCPU);  // synchronises the C3 stream
+    uint32_t fault = 0;
+    checkAbi(c3cu_fault_status(&fault), describe().c_str());
+  }
+  return outs;
+}
+
+// ---------------------------------------------------------------------------- region
+std::string CudaRegionKernel::describe() const {
+  std::ostringstream ss;
+  ss << "region MatMul+Add+ReLU M=" << M_ << " K=" << K_ << " N=" << N_ << " bias=" << bias_numel_
+     << (trans_b_ ? " B^T" : "");
+  return ss.str();
+}
+
+std::vector<Tensor> CudaRegionKernel::run(const std::vector<Tensor>& in) {
+  const Tensor& X = in[pos_[0]];
+  const Tensor& B = in[pos_[1]];
+  const Tensor& b = in[pos_[2]];
+  expectShape(X, {M_, K_}, "region X");
+  expectShape(B, trans_b_ ? std::vector<size_t>{N_, K_} : std::vector<size_t>{K_, N_}, "region B");
+  if (b.numel() != bias_numel_) throw std::runtime_error("region: bias size mismatch");
+  const size_t words = (N_ + 31) / 32;
+  Tensor mask = newDevice({M_, words}, DType::kInt32);
+  const bool bf16_in = X.dtype() == DType::kBF16 && B.dtype() == DType::kBF16;
+  const bool f32_in = X.dtype() == DType::kFloat && B.dtype() == DType::kFloat;
+  if (f32_in && precision_ == Precision::kExactF32) {
+    Tensor bf = convert(b, DType::kFloat);
+    Tensor Y = newDevice({M_, N_}, DType::kFloat);
+    checkAbi(c3cu_region_fwd_f32(static_cast<const float*>(X.data()), static_cast<const float*>(B.data()),
+                                 static_cast<const float*>(bf.data()), static_cast<int64_t>(bias_numel_),
+                                 static_cast<float*>(Y.data()), nullptr,
+                                 static_cast<uint32_t*>(mask.data()), M_, K_, N_, trans_b_ ? 1 : 0,
+                                 stream()),
+             "region_fwd_f32");
+    return {Y, mask};
+  }
+  if (!bf16_in && !f32_in) throw std::runtime_error("region: X and B must share a dtype (bf16 or fp32)");
+  if (bias_numel_ != N_)
+    throw std::runtime_error("region: the tensor-core epilogue needs one bias per output column");
+  Tensor Xb = convert(X, DType::kBF16), Bb = convert(B, DType::kBF16), bf = convert(b, DType::kFloat);
+  Tensor Y = newDevice({M_, N_}, DType::kBF16);
+  checkAbi(c3cu_linear_bias_relu_fwd(Xb.data(), Bb.data(), static_cast<const float*>(bf.data()), Y.data(),
+                                     static_cast<uint32_t*>(mask.data()), M_, N_, K_,
+                                     trans_b_ ? C3CU_W_NK : C3CU_W_KN, stream()),
+           "linear_bias_relu_fwd");
+  if (f32_in) return {convert(Y, DType::kFloat), mask};
+  return {Y, mask};
+}
+
+// ---------------------------------------------------------------------------- matmul
+std::string CudaMatMulKernel::describe() const {
+  std::ostringstream ss;
+  ss << "matmul M=" << M_ << " K=" << K_ << " N=" << N_ << (trans_a_ ? " A^T" : "")
+     << (trans_b_ ? " B^T" : "") << (has_bias_ ? " +bias" : "") << " act=" << act_;
+  return ss.str();
+}
+
+std::vector<Tensor> CudaMatMulKernel::run(const std::vector<Tensor>& in) {
+  const Tensor& A = in[pos_[0]];
+  const Tensor& B = in[pos_[1]];
+  expectShape(A, trans_a_ ? std::vector<size_t>{K_, M_} : std::vector<size_t>{M_, K_}, "matmul A");
+  expectShape(B, trans_b_ ? std::vector<size_t>{N_, K_} : std::vector<size_t>{K_, N_}, "matmul B");
+  const bool bf16_in = A.dtype() == DType::kBF16 && B.dtype() == DType::kBF16;
+  const bool f32_in = A.dtype() == DType::kFloat && B.dtype() == DType::kFloat;
+  if (!bf16_in && !f32_in) throw std::runtime_error("matmul: A and B must share a dtype (bf16 or fp32)");
+  const bool epilogue = has_bias_ || act_ != 0;
+  Tensor T;
+  if (f32_in && precision_ == Precision::kExactF32) {
+    T = newDevice({M_, N_}, DType::kFloat);
+    checkAbi(c3cu_matmul_f32(static_cast<const float*>(A.data()), static_cast<const float*>(B.data()),
+                             static_cast<float*>(T.data()), M_, K_, N_, trans_a_ ? 1 : 0,
+                             trans_b_ ? 1 : 0, nullptr, 0, 0, stream()),
+             "matmul_f32");
+  } else {
+    Tensor Ab = convert(A, DType::kBF16), Bb = convert(B, DType::kBF16);
+    // bf16 inputs without an epilogue keep a bf16 result; otherwise fp32 feeds the epilogue.
+    const bool out_bf16 = bf16_in && !epilogue;
+    T = newDevice({M_, N_}, out_bf16 ? DType::kBF16 : DType::kFloat);
+    // Operand majors: A stored [M][K] (K-major) or [K][M] (MN-major); B stored [N][K]
+    // (K-major, trans_b) or [K][N] (MN-major).
+    checkAbi(c3cu_gemm_bf16(Ab.data(), trans_a_ ? M_ : K_, trans_a_ ? 1 : 0, Bb.data(),
+                            trans_b_ ? K_ : N_, trans_b_ ? 0 : 1, T.data(), N_,
+                            out_bf16 ? C3CU_EPI_STORE_BF16 : C3CU_EPI_STORE_F32, nullptr, nullptr, 0,
+                            M_, N_, K_, stream()),
+             "gemm_bf16");
+  }
+  if (!epilogue) return {T};
+  // T then the elementwise epilogue, as the reference evaluates the FusedNode after the
+  // matmul: s = T + bias[idx % numel(bias)]; out = act(s).
+  std::vector<uint8_t> code;
+  std::vector<Tensor> ins{T};
+  int cur = 0;
+  if (has_bias_) {
+    ins.push_back(in[pos_[2]]);
+    code.insert(code.end(), {C3CU_EW_ADD, 2, 0, 1});
+    cur = 2;
+  }
+  if (act_ == 1) code.insert(code.end(), {C3CU_EW_RELU, 3, static_cast<uint8_t>(cur), 0});
+  if (act_ == 2) code.insert(code.end(), {C3CU_EW_SIGMOID, 3, static_cast<uint8_t>(cur), 0});
+  if (act_ == 3) code.insert(code.end(), {C3CU_EW_TANH, 3, static_cast<uint8_t>(cur), 0});
+  const int out_reg = act_ ? 3 : cur;
+  Tensor out = runProgram(ins, code, {}, out_reg, {M_, N_});
+  if (bf16_in) return {convert(out, DType::kBF16)};
+  return {out};
+}
+
+// ---------------------------------------------------------------------------- relu backward
+std::vector<Tensor> CudaReluBackwardKernel::run(const std::vector<Tensor>& in) {
+  const Tensor& grad = in[pos_[0]];
+  const Tensor& x = in[pos_[1]];
+  if (x.dtype() == DType::kInt32) {
+    // x is the forward's bit mask: dZ = float(bit) * grad via the fused mask kernel.
+    if (grad.shape().size() != 2) throw std::runtime_error("relu backward: 2-D gradient expected with a mask");
+    const size_t M = grad.shape()[0], N = grad.shape()[1];
+    expectShape(x, {M, (N + 31) / 32}, "relu backward mask");
+    Tensor g = convert(grad, DType::kBF16);
+    Tensor dz = newDevice({M, N}, DType::kBF16);
+    Tensor db = newDevice({N}, DType::kFloat);
+    const size_t ws_bytes = c3cu_relu_mask_db_workspace(M, N);
+    Tensor ws = newDevice({ws_bytes / 4 + 1}, DType::kInt32);
+    checkAbi(c3cu_relu_mask_db(g.data(), static_cast<const uint32_t*>(x.data()), dz.data(),
+                               static_cast<float*>(db.data()), M, N, ws.data(), ws.nbytes(), stream()),
+             "relu_mask_db");
+    return {grad.dtype() == DType::kBF16 ? dz : convert(dz, DType::kFloat)};
+  }
+  if (x.shape() != grad.shape()) throw std::runtime_error("relu backward: x and grad shapes differ");
+  // Mul(Gt(x, 0), grad): r2 = 0; r3 = x > r2; r4 = r3 * grad
+  const std::vector<uint8_t> code{C3CU_EW_CONST, 2, 0, 0, C3CU_EW_GT, 3, 1, 2, C3CU_EW_MUL, 4, 3, 0};
+  Tensor out = runProgram({grad, x}, code, {0.0f}, 4, grad.shape());
+  return {grad.dtype() == DType::kBF16 ? convert(out, DType::kBF16) : out};
+}
+
+// ---------------------------------------------------------------------------- sum reduce
+std::vector<Tensor> CudaSumReduceKernel::run(const std::vector<Tensor>& in) {
+  expectShape(in[0], {M_, N_}, "sum_reduce");
+  Tensor f = convert(in[0], DType::kFloat);
+  Tensor out = newDevice({N_}, DType::kFloat);
+  checkAbi(c3cu_sum_rows_f32_exact(static_cast<const float*>(f.data()), static_cast<float*>(out.data()),
+                                   M_, N_, stream()),
+           "sum_rows_f32_exact");
+  return {in[0].dtype() == DType::kBF16 ? convert(out, DType::kBF16) : out};
+}
+
+// ---------------------------------------------------------------------------- elementwise
+std::string CudaElementwiseKernel::describe() const {
+  return "elementwise program (" + std::to_string(code_.size() / 4) + " instructions)";
+}
+
+std::vector<Tensor> CudaElementwiseKernel::run(const std::vector<Tensor>& in) {
+  bool all_bf16 = true;
+  for (const auto& t : in) all_bf16 = all_bf16 && t.dtype() == DType::kBF16;
+  Tensor out = runProgram(in, code_, consts_, out_reg_, out_shape_);
+  return {all_bf16 && !in.empty() ? convert(out, DType::kBF16) : out};
+}
+
+// ---------------------------------------------------------------------------- lowering
+namespace {
+
+template <typename T>
+bool is(const Graph& g, size_t id) {
+  return std::holds_alternative<T>(g.node(id).op);
+}
+
+long inputPos(const Graph& g, size_t id) {
+  const auto& ins = g.inputs();
+  auto it = std::find(ins.begin(), ins.end(), id);
+  return it == ins.end() ? -1 : static_cast<long>(it - ins.begin());
+}
+
+std::shared_ptr<CudaKernelBase> lowerMatMul(const Graph& g, const std::vector<size_t>& cn,
+                                            const CompileOptions& o, const std::string& key) {
+  size_t i = 0;
+  std::map<size_t, size_t> transposed;  // transpose node -> its graph input
+  while (i < cn.size() && is<TransposeNode>(g, cn[i])) {
+    const auto& n = g.node(cn[i]);
+    const auto& t = std::get<TransposeNode>(n.op);
+    if (n.inputs.size() != 1 || inputPos(g, n.inputs[0]) < 0 || n.out_desc.shape.size() != 2 ||
+        !((t.dim0 == 0 && t.dim1 == 1) || (t.dim0 == 1 && t.dim1 == 0)))
+      return nullptr;
+    transposed[cn[i]] = n.inputs[0];
+    ++i;
+  }
+  if (i >= cn.size() || !is<MatMulNode>(g, cn[i])) return nullptr;
+  const auto& mm = g.node(cn[i]);
+  if (mm.inputs.size() != 2 || mm.out_desc.shape.size() != 2) return nullptr;
+  auto operand = [&](size_t id, bool& trans) -> long {
+    auto it = transposed.find(id);
+    trans = it != transposed.end();
+    return inputPos(g, trans ? it->second : id);
+  };
+  bool ta = false, tb = false;
+  const long pa = operand(mm.inputs[0], ta), pb = operand(mm.inputs[1], tb);
+  if (pa < 0 || pb < 0) return nullptr;
+  const size_t M = mm.out_desc.shape[0], N = mm.out_desc.shape[1];
+  const auto& lhs_shape = g.node(mm.inputs[0]).out_desc.shape;
+  if (lhs_shape.size() != 2) return nullptr;
+  const size_t K = lhs_shape[1];
+  size_t last = cn[i];
+  ++i;
+  long pbias = -1;
+  size_t bias_numel = 0;
+  if (i < cn.size() && is<AddNode>(g, cn[i])) {
+    const auto& add = g.node(cn[i]);
+    if (add.inputs.size() != 2) return nullptr;
+    const size_t other = add.inputs[0] == last ? add.inputs[1] : add.inputs[1] == last ? add.inputs[0] : SIZE_MAX;
+    if (other == SIZE_MAX || (pbias = inputPos(g, other)) < 0) return nullptr;
+    bias_numel = g.node(other).out_desc.numel ? g.node(other).out_desc.numel
+                                              : TensorDesc::computeNumel(g.node(other).out_desc.shape);
+    if (bias_numel == 0 || (M * N) % bias_numel != 0) return nullptr;
+    last = cn[i];
+    ++i;
+  }
+  int act = 0;
+  if (i < cn.size()) {
+    const auto& a = g.node(cn[i]);
+    if (a.inputs.size() != 1 || a.inputs[0] != last) return nullptr;
+    if (is<ReLUNode>(g, cn[i])) act = 1;
+    else if (is<SigmoidNode>(g, cn[i])) act = 2;
+    else if (is<TanhNode>(g, cn[i])) act = 3;
+    else return nullptr;
+    last = cn[i];
+    ++i;
+  }
+  if (i != cn.size() || g.outputs()[0] != last) return nullptr;
+  std::vector<size_t> pos{static_cast<size_t>(pa), static_cast<size_t>(pb)};
+  if (pbias >= 0) pos.push_back(static_cast<size_t>(pbias));
+  if (pbias >= 0 && act == 1 && !ta)
+    return std::make_shared<CudaRegionKernel>(key, o.fp32_precision, M, K, N, bias_numel, tb, pos);
+  return std::make_shared<CudaMatMulKernel>(key, o.fp32_precision, M, K, N, ta, tb, pbias >= 0,
+                                            bias_numel, act, pos);
+}
+
+std::shared_ptr<CudaKernelBase> lowerReluBackward(const Graph& g, const std::vector<size_t>& cn,
+                                                  const CompileOptions& o, const std::string& key) {
+  if (cn.size() != 2 || !is<GtNode>(g, cn[0]) || !is<MulNode>(g, cn[1])) return nullptr;
+  const auto& gt = g.node(cn[0]);
+  const auto& mul = g.node(cn[1]);
+  if (gt.inputs.size() != 2 || !g.isConst(gt.inputs[1]) ||
+      std::get<ConstNode>(g.node(gt.inputs[1]).op).value != 0.0)
+    return nullptr;
+  const long px = inputPos(g, gt.inputs[0]);
+  if (mul.inputs.size() != 2) return nullptr;
+  const size_t grad = mul.inputs[0] == cn[0] ? mul.inputs[1] : mul.inputs[1] == cn[0] ? mul.inputs[0] : SIZE_MAX;
+  const long pg = grad == SIZE_MAX ? -1 : inputPos(g, grad);
+  if (px < 0 || pg < 0 || g.outputs()[0] != cn[1]) return nullptr;
+  return std::make_shared<CudaReluBackwardKernel>(key, o.fp32_precision, mul.out_desc.shape,
+                                                  std::vector<size_t>{static_cast<size_t>(pg),
+                                                                      static_cast<size_t>(px)});
+}
+
+std::shared_ptr<CudaKernelBase> lowerSumReduce(const Graph& g, const std::vector<size_t>& cn,
+                                               const CompileOptions& o, const std::string& key) {
+  if (cn.size() != 1 || !is<SumReduceNode>(g, cn[0])) return nullptr;
+  const auto& n = g.node(cn[0]);
+  const auto& s = std::get<SumReduceNode>(n.op);
+  const auto& in_shape = g.node(n.inputs[0]).out_desc.shape;
+  if (s.axis != 0 || in_shape.size() != 2 || inputPos(g, n.inputs[0]) != 0 || g.inputCount() != 1)
+    return nullptr;
+  return std::make_shared<CudaSumReduceKernel>(key, o.fp32_precision, in_shape[0], in_shape[1]);
+}
+
+std::shared_ptr<CudaKernelBase> lowerElementwise(const Graph& g, const std::vector<size_t>& cn,
+                                                 const CompileOptions& o, const std::string& key) {
+  if (g.inputCount() > C3CU_EW_MAX_INPUTS) return nullptr;
+  const size_t out_id = g.outputs()[0];
+  const size_t n_out = TensorDesc::computeNumel(g.node(out_id).out_desc.shape);
+  bool broadcast = false;
+  for (size_t in : g.inputs())
+    broadcast = broadcast || TensorDesc::computeNumel(g.node(in).out_desc.shape) < n_out;
+  // last use of every node, to recycle registers
+  std::map<size_t, size_t> last_use;
+  for (size_t k = 0; k < cn.size(); ++k)
+    for (size_t in : g.node(cn[k]).inputs) last_use[in] = k;
+  std::map<size_t, int> reg;
+  std::vector<bool> busy(16, false);
+  for (size_t i = 0; i < g.inputCount(); ++i) {
+    reg[g.inputs()[i]] = static_cast<int>(i);
+    busy[i] = true;
+  }
+  std::vector<uint8_t> code;
+  std::vector<float> consts;
+  auto alloc = [&]() -> int {
+    for (int r = 0; r < 16; ++r)
+      if (!busy[r]) {
+        busy[r] = true;
+        return r;
+      }
+    return -1;
+  };
+  auto emit = [&](int opc, int d, int a, int b) {
+    code.insert(code.end(), {static_cast<uint8_t>(opc), static_cast<uint8_t>(d), static_cast<uint8_t>(a),
+                             static_cast<uint8_t>(b)});
+  };
+  auto operand = [&](size_t id) -> int {
+    auto it = reg.find(id);
+    if (it != reg.end()) return it->second;
+    if (!g.isConst(id) || consts.size() >= 16) return -1;
+    const int r = alloc();
+    if (r < 0) return -1;
+    consts.push_back(static_cast<float>(std::get<ConstNode>(g.node(id).op).value));
+    emit(C3CU_EW_CONST, r, static_cast<int>(consts.size() - 1), 0);
+    reg[id] = r;
+    return r;
+  };
+  for (size_t k = 0; k < cn.size(); ++k) {
+    const auto& n = g.node(cn[k]);
+    int opc = 0;
+    bool binary = true;
+    if (is<AddNode>(g, n.id)) opc = C3CU_EW_ADD;
+    else if (is<SubNode>(g, n.id)) opc = C3CU_EW_SUB;
+    else if (is<MulNode>(g, n.id)) opc = C3CU_EW_MUL;
+    else if (is<DivNode>(g, n.id)) opc = broadcast ? C3CU_EW_DIV_NANZ : C3CU_EW_DIV;
+    else if (is<GtNode>(g, n.id)) opc = C3CU_EW_GT;
+    else {
+      binary = false;
+      if (is<NegNode>(g, n.id)) opc = C3CU_EW_NEG;
+      else if (is<ReLUNode>(g, n.id)) opc = C3CU_EW_RELU;
+      else if (is<SigmoidNode>(g, n.id)) opc = C3CU_EW_SIGMOID;
+      else if (is<TanhNode>(g, n.id)) opc = broadcast ? C3CU_EW_TANH_EXP : C3CU_EW_TANH;
+      else if (is<ExpNode>(g, n.id)) opc = C3CU_EW_EXP;
+      else if (is<LogNode>(g, n.id)) opc = C3CU_EW_LOG;
+      else return nullptr;
+    }
+    if (n.inputs.size() != (binary ? 2u : 1u)) return nullptr;
+    const int a = operand(n.inputs[0]);
+    const int b = binary ? operand(n.inputs[1]) : 0;
+    if (a < 0 || b < 0) return nullptr;
+    // free registers whose last use is this node (never the graph inputs' home registers
+    // before their last use)
+    for (size_t in : n.inputs)
+      if (last_use[in] == k && reg.count(in)) busy[reg[in]] = false;
+    const int d = alloc();
+    if (d < 0 || code.size() / 4 >= C3CU_EW_MAX_INSTR) return nullptr;
+    emit(opc, d, a, b);
+    reg[n.id] = d;
+  }
+  if (code.size() / 4 > C3CU_EW_MAX_INSTR) return nullptr;
+  return std::make_shared<CudaElementwiseKernel>(key, o.fp32_precision, g.node(out_id).out_desc.shape,
+                                                 std::move(code), std::move(consts), reg[out_id],
+                                                 g.inputCount());
+}
+
+}  // namespace
+
+std::shared_ptr<CudaKernelBase> lowerGraph(const Graph& graph, const CompileOptions& options,
+                                           const std::string& key) {
+  const Graph g = graph.eliminateDeadCode();
+  if (!g.isValid()) throw std::runtime_error("compile: invalid graph");
+  if (g.outputCount() != 1) throw std::runtime_error("compile: exactly one graph output is supported");
+  const auto cn = g.computeNodes();
+  if (cn.empty()) throw std::runtime_error("compile: graph has no compute node (identity)");
+  for (auto* fn : {lowerMatMul, lowerReluBackward, lowerSumReduce, lowerElementwise})
+    if (auto k = fn(g, cn, options, key)) return k;
+  throw std::runtime_error("compile: no B200 kernel implements this graph:\n" + g.toString());
+}
+
+}  // namespace c3
+}  // namespace ct

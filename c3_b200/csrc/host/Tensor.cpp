@@ -1,0 +1,86 @@
+#include "Tensor.h"
+
+#include <cstdlib>
+#include <cstring>
+
+#include "C3/CudaRuntime.h"
+
+struct Tensor::Storage {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DeviceType device = DeviceType::kCPU;
+  bool owned = true;
+  ~Storage() {
+    if (!owned || !ptr) return;
+    if (device == DeviceType::kCUDA)
+      ct::c3::cuda::freeDevice(ptr);
+    else
+      std::free(ptr);
+  }
+};
+
+Tensor::Tensor(ShapeTag, const std::vector<size_t>& shape, DType dtype, DeviceType device)
+    : shape_(shape), dtype_(dtype), device_(device) {
+  auto st = std::make_shared<Storage>();
+  st->bytes = numel() * dtypeSize(dtype);
+  st->device = device;
+  if (device == DeviceType::kCUDA) {
+    st->ptr = ct::c3::cuda::allocDevice(st->bytes);
+  } else {
+    const size_t rounded = ((st->bytes + 63) / 64) * 64;
+    st->ptr = std::aligned_alloc(64, rounded > 0 ? rounded : 64);
+    if (!st->ptr) throw std::bad_alloc();
+  }
+  storage_ = std::move(st);
+}
+
+Tensor Tensor::wrap(void* data, const std::vector<size_t>& shape, DType dtype, DeviceType device) {
+  Tensor t;
+  t.shape_ = shape;
+  t.dtype_ = dtype;
+  t.device_ = device;
+  auto st = std::make_shared<Storage>();
+  st->ptr = data;
+  st->bytes = t.numel() * dtypeSize(dtype);
+  st->device = device;
+  st->owned = false;
+  t.storage_ = std::move(st);
+  return t;
+}
+
+size_t Tensor::numel() const {
+  size_t n = 1;
+  for (size_t d : shape_) n *= d;
+  return n;
+}
+
+const void* Tensor::data() const { return storage_ ? storage_->ptr : nullptr; }
+void* Tensor::data() { return storage_ ? storage_->ptr : nullptr; }
+
+Tensor Tensor::reshape(const std::vector<size_t>& shape) const {
+  size_t n = 1;
+  for (size_t d : shape) n *= d;
+  if (n != numel()) throw std::runtime_error("reshape: element count mismatch");
+  Tensor t = *this;
+  t.shape_ = shape;
+  return t;
+}
+
+Tensor Tensor::to(DeviceType device) const {
+  if (!defined()) return Tensor();
+  Tensor out(ShapeTag{}, shape_, dtype_, device);
+  const size_t bytes = nbytes();
+  if (bytes == 0) return out;
+  if (device_ == DeviceType::kCPU && device == DeviceType::kCPU) {
+    std::memcpy(out.data(), data(), bytes);
+    return out;
+  }
+  cudaStream_t s = ct::c3::cuda::currentStream();
+  const cudaMemcpyKind kind = device_ == DeviceType::kCPU    ? cudaMemcpyHostToDevice
+                              : device == DeviceType::kCPU ? cudaMemcpyDeviceToHost
+                                                           : cudaMemcpyDeviceToDevice;
+  ct::c3::cuda::checkCuda(cudaMemcpyAsync(out.data(), data(), bytes, kind, s), "Tensor::to");
+  if (device == DeviceType::kCPU || device_ == DeviceType::kCPU)
+    ct::c3::cuda::checkCuda(cudaStreamSynchronize(s), "Tensor::to: synchronize");
+  return out;
+}

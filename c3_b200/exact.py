@@ -1,0 +1,54 @@
+"""Bit-exact fp32 kernels (CUDA cores) restating the reference's fp32 loops: the c3.matmul
+sequential-k reduction (src/C3/C3DialectLowering.cpp:467-610), the MatMul+Add+ReLU region
+(src/C3/MLIRKernelGen.cpp:610-768) and SumReduce axis 0 (src/C3/C3DialectLowering.cpp:382-465)."""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .linear import _p, _stream
+
+
+def _f32(t, name):
+    if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+        raise _lib.C3CUError(-1, name, "expected a contiguous fp32 CUDA tensor")
+
+
+def matmul(A: torch.Tensor, B: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
+           bias: torch.Tensor | None = None, act: int = 0) -> torch.Tensor:
+    """out = act(bias_init + sum_k a(i,k) b(k,j)); A [M,K] ([K,M] if trans_a), B [K,N] ([N,K] if trans_b)."""
+    _f32(A, "A")
+    _f32(B, "B")
+    M, K = (A.shape[1], A.shape[0]) if trans_a else (A.shape[0], A.shape[1])
+    N = B.shape[0] if trans_b else B.shape[1]
+    out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    rc = _lib.load().c3cu_matmul_f32(_p(A), _p(B), _p(out), M, K, N, int(trans_a), int(trans_b), _p(bias),
+                                     0 if bias is None else bias.numel(), act, _stream(A.device))
+    _lib.check(rc, "c3cu_matmul_f32")
+    return out
+
+
+def region_forward(X: torch.Tensor, B: torch.Tensor, b: torch.Tensor, trans_b: bool = False,
+                   want_z: bool = False):
+    """(out, z, mask) of the fp32 region: z = X B + b[idx % numel(b)], out = max(z, 0)."""
+    _f32(X, "X")
+    _f32(B, "B")
+    _f32(b, "b")
+    M, K = X.shape
+    N = B.shape[0] if trans_b else B.shape[1]
+    out = torch.empty((M, N), dtype=torch.float32, device=X.device)
+    z = torch.empty_like(out) if want_z else None
+    mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=X.device)
+    rc = _lib.load().c3cu_region_fwd_f32(_p(X), _p(B), _p(b), b.numel(), _p(out), _p(z), _p(mask), M, K, N,
+                                         int(trans_b), _stream(X.device))
+    _lib.check(rc, "c3cu_region_fwd_f32")
+    return out, z, mask
+
+
+def sum_rows(x: torch.Tensor) -> torch.Tensor:
+    _f32(x, "x")
+    M, N = x.shape
+    out = torch.empty(N, dtype=torch.float32, device=x.device)
+    rc = _lib.load().c3cu_sum_rows_f32_exact(_p(x), _p(out), M, N, _stream(x.device))
+    _lib.check(rc, "c3cu_sum_rows_f32_exact")
+    return out

@@ -102,6 +102,26 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,
                    int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream);
 
+/* ------------------------------------------------------------------ exact fp32 (CUDA cores)
+ * Bit-exact restatements of the reference's fp32 loops: every output element is reduced
+ * over k in ascending order with separate round-to-nearest multiply and add.
+ * c3cu_matmul_f32: out[M][N] = act(bias-init + sum_k a(i,k) b(k,j)) with
+ *   a(i,k) = transA ? A[k*M+i] : A[i*K+k],  b(k,j) = transB ? B[j*K+k] : B[k*N+j],
+ *   bias-init = bias ? bias[bias_numel == 1 ? 0 : j] : 0,  act: 0 none, 1 ReLU, 2 sigmoid, 3 tanh
+ *   (c3.matmul, src/C3/C3DialectLowering.cpp:467-610).
+ * c3cu_region_fwd_f32: T = sum (from 0); s = T + bias[idx % bias_numel]; out = max(s, 0);
+ *   z (optional) = s; mask (optional) as in c3cu_linear_bias_relu_fwd
+ *   (MatMul + FusedNode{Add, ReLU}, src/C3/MLIRKernelGen.cpp:610-768). */
+int c3cu_matmul_f32(const float* A, const float* B, float* out, int64_t M, int64_t K, int64_t N,
+                    int transA, int transB, const float* bias, int64_t bias_numel, int act,
+                    c3cu_stream_t stream);
+int c3cu_region_fwd_f32(const float* X, const float* B, const float* bias, int64_t bias_numel,
+                        float* out, float* z, uint32_t* mask, int64_t M, int64_t K, int64_t N,
+                        int transB, c3cu_stream_t stream);
+/* Column sums in the reference's order (rows ascending), bit-exact; no workspace. */
+int c3cu_sum_rows_f32_exact(const float* in, float* out, int64_t M, int64_t N,
+                            c3cu_stream_t stream);
+
 /* ------------------------------------------------------------------ elementwise chains
  * The chain relu((A + B) * C - A) / (1 + exp(-B)) over n fp32 elements, one pass. */
 int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* out, int64_t n,
@@ -131,6 +151,10 @@ int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* ou
 int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,
                     const uint8_t* code, int n_instr, const float* constants, int n_constants,
                     int out_reg, float* out, int64_t n, c3cu_stream_t stream);
+
+/* out[i] = in[i] converted between C3CU_DTYPE_F32 and C3CU_DTYPE_BF16 (round to nearest even). */
+int c3cu_convert(const void* in, int in_dtype, void* out, int out_dtype, int64_t n,
+                 c3cu_stream_t stream);
 
 /* db[n] = sum over rows of a fp32 matrix [M][N] (axis 0), deterministic order. */
 size_t c3cu_sum_rows_f32_workspace(int64_t M, int64_t N);

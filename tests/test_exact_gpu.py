@@ -1,0 +1,65 @@
+"""The fp32 path reproduces the reference's arithmetic bit for bit (max_diff = 0, the
+reference's own parity claim for MatMul/Add): sequential-k fmul/fadd GEMM, the region's
+T + b then maxnum, and the row-ordered SumReduce."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from c3_b200 import exact
+from tests.helpers import unpack_mask
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 784, 256), (128, 256, 128), (128, 128, 10), (1, 1, 1), (65, 33, 17), (300, 1000, 70)]
+
+
+def _rand(shape, seed, lo=-1.0, hi=1.0):
+    return (torch.rand(shape, generator=torch.Generator().manual_seed(seed)) * (hi - lo) + lo).float()
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+def test_matmul_bit_exact(cuda_device, M, K, N, ta, tb):
+    A = _rand((K, M) if ta else (M, K), M + K)
+    B = _rand((N, K) if tb else (K, N), K + N)
+    out = exact.matmul(A.to(cuda_device), B.to(cuda_device), ta, tb).cpu().numpy()
+    ref = oracle.matmul(A.numpy(), B.numpy(), transA=ta, transB=tb)
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_matmul_bias_init_and_act(cuda_device, act):
+    M, K, N = 64, 96, 48
+    A, B, bias = _rand((M, K), 1), _rand((K, N), 2), _rand((N,), 3)
+    out = exact.matmul(A.to(cuda_device), B.to(cuda_device), bias=bias.to(cuda_device), act=act).cpu().numpy()
+    ref = oracle.matmul(A.numpy(), B.numpy(), bias=bias.numpy(), act=act)
+    if act in (0, 1):
+        assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+    else:  # expf / tanhf come from different libms: a few ulp
+        assert np.abs(out - ref).max() <= 4e-7 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_region_forward_bit_exact(cuda_device, M, K, N):
+    X, B, b = _rand((M, K), 10, 0, 1), _rand((K, N), 11, -0.1, 0.1), _rand((N,), 12, -0.1, 0.1)
+    out, z, mask = exact.region_forward(X.to(cuda_device), B.to(cuda_device), b.to(cuda_device), want_z=True)
+    ref, zref = oracle.region_fwd(X.numpy(), B.numpy(), b.numpy())
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    assert np.array_equal(z.cpu().numpy().view(np.uint32), zref.view(np.uint32))
+    assert np.array_equal(unpack_mask(mask.cpu().numpy().view(np.uint32), N), zref > 0)
+
+
+def test_region_forward_scalar_bias_broadcast(cuda_device):
+    X, B, b = _rand((33, 20), 20), _rand((20, 12), 21), _rand((1,), 22)
+    out, _, _ = exact.region_forward(X.to(cuda_device), B.to(cuda_device), b.to(cuda_device))
+    ref, _ = oracle.region_fwd(X.numpy(), B.numpy(), b.numpy())
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("M,N", [(128, 256), (16384, 10), (1, 7), (1000, 1000)])
+def test_sum_rows_bit_exact(cuda_device, M, N):
+    x = _rand((M, N), M * 7 + N)
+    out = exact.sum_rows(x.to(cuda_device)).cpu().numpy()
+    ref = oracle.sum_reduce(x.numpy(), 0)
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
