@@ -10,6 +10,7 @@
 // explicit round-to-nearest intrinsics (__fadd_rn, __fmul_rn, ...) so that the compiler
 // cannot contract them into FMAs: the reference evaluates each node as a separate fp32
 // operation (src/C3/MLIRKernelGen.cpp:394-768), and the kernels keep that order.
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -339,6 +340,46 @@ int grid_for(int64_t work_items, int threads) {
 }  // namespace ew
 }  // namespace c3cu
 
+// ------------------------------------------------------------------ allocation-free scratch
+// Scratch of c3cu_relu_mask_db_noalloc: a fixed array in device global memory that the
+// library owns. Every GPU that loads the library holds C3CU_NOALLOC_SCRATCH_BYTES of it
+// until the process exits. Host code must not pass `g_noalloc_scratch` itself to a kernel
+// (on the host that name is a stand-in, not a device address): the address is looked up
+// once per device with cudaGetSymbolAddress and cached.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[C3CU_NOALLOC_SCRATCH_BYTES];
+
+namespace c3cu {
+namespace ew {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device; the first call on a device
+// performs the lookup (so it should happen before any stream capture).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "relu_mask_db_noalloc: cudaGetDevice");
+  if (rc != C3CU_OK) return rc;
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("relu_mask_db_noalloc: device ordinal %d out of range", dev);
+    return C3CU_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                     "relu_mask_db_noalloc: cudaGetSymbolAddress of the scratch array");
+    if (rc != C3CU_OK) return rc;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return C3CU_OK;
+}
+}  // namespace
+}  // namespace ew
+}  // namespace c3cu
+
 extern "C" {
 
 size_t c3cu_relu_mask_db_workspace(int64_t M, int64_t N) { return c3cu::ew::colsum_workspace(M, N); }
@@ -348,6 +389,30 @@ int c3cu_relu_mask_db(const void* dY, const uint32_t* mask, void* dZ, float* db,
   int rc = c3cu::require_sm100();
   if (rc != C3CU_OK) return rc;
   return c3cu::ew::launch_colsum<true>(dY, mask, dZ, db, M, N, workspace, workspace_bytes,
+                                       static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_relu_mask_db_noalloc(const void* dY, const uint32_t* mask, void* dZ, float* db,
+                              int64_t M, int64_t N, c3cu_stream_t stream) {
+  int rc = c3cu::require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (M < 0 || N < 0) {
+    c3cu::set_error("relu_mask_db_noalloc: negative size");
+    return C3CU_ERR_INVALID;
+  }
+  const size_t need = c3cu::ew::colsum_workspace(M, N);
+  if (need > C3CU_NOALLOC_SCRATCH_BYTES) {
+    c3cu::set_error("relu_mask_db_noalloc: M=%lld N=%lld needs %zu bytes of scratch, more than the "
+                    "%d-byte built-in array; use c3cu_relu_mask_db with a caller workspace",
+                    (long long)M, (long long)N, need, C3CU_NOALLOC_SCRATCH_BYTES);
+    return C3CU_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  rc = c3cu::ew::noalloc_scratch(&scratch);
+  if (rc != C3CU_OK) return rc;
+  // launch_colsum clears the ticket counters in the scratch before the kernel; the partial
+  // sums are fully written before they are read, so stale contents from earlier calls are harmless.
+  return c3cu::ew::launch_colsum<true>(dY, mask, dZ, db, M, N, scratch, C3CU_NOALLOC_SCRATCH_BYTES,
                                        static_cast<cudaStream_t>(stream));
 }
 

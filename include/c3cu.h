@@ -86,6 +86,21 @@ size_t c3cu_relu_mask_db_workspace(int64_t M, int64_t N);
 int c3cu_relu_mask_db(const void* dY, const uint32_t* mask, void* dZ, float* db, int64_t M,
                       int64_t N, void* workspace, size_t workspace_bytes, c3cu_stream_t stream);
 
+/* The same pre-pass for callers that cannot allocate device memory: a host framework whose
+ * allocator owns every byte of device memory and forbids side allocations, or a latency-
+ * critical path where cudaMalloc's implicit device synchronisation is unacceptable. No
+ * counterpart exists in the reference (its CPU kernels take a host scratch pointer).
+ * Scratch is a fixed array of C3CU_NOALLOC_SCRATCH_BYTES in device memory that the library
+ * owns (every GPU that loads the library holds it until exit); the call needs
+ * c3cu_relu_mask_db_workspace(M, N) <= C3CU_NOALLOC_SCRATCH_BYTES (for N = 4096 up to
+ * M = 130560 rows) and returns C3CU_ERR_WORKSPACE beyond that. It allocates nothing. Its
+ * first call on a device looks up the array's device address, so make that first call
+ * before any stream capture. All calls share the one array: calls that overlap on the GPU
+ * (concurrent streams, or several host threads) race and must be serialised by the caller. */
+#define C3CU_NOALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
+int c3cu_relu_mask_db_noalloc(const void* dY, const uint32_t* mask, void* dZ, float* db,
+                              int64_t M, int64_t N, c3cu_stream_t stream);
+
 /* dX = dZ * W (C3CU_W_NK, W[N][K]) or dZ * B^T (C3CU_W_KN, B[K][N]); bf16 out [M][K]. */
 int c3cu_gemm_dx(const void* dZ, const void* W, void* dX, int64_t M, int64_t N, int64_t K,
                  int w_layout, c3cu_stream_t stream);
