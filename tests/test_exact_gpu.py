@@ -63,3 +63,26 @@ def test_sum_rows_bit_exact(cuda_device, M, N):
     out = exact.sum_rows(x.to(cuda_device)).cpu().numpy()
     ref = oracle.sum_reduce(x.numpy(), 0)
     assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_exact_kernels_reproduce_golden_vectors(cuda_device):
+    """The GPU fp32 path against the golden vectors of the independent restatement."""
+    import json
+    from pathlib import Path
+    gold = json.loads((Path(__file__).resolve().parent / "golden" / "golden.json").read_text())
+    arr = lambda v, s=None: (np.array(v, np.uint32).view(np.float32).reshape(s) if s else
+                             np.array(v, np.uint32).view(np.float32))
+    c = gold["region_fwd"]
+    M, K, N = c["M"], c["K"], c["N"]
+    out, z, _ = exact.region_forward(torch.from_numpy(arr(c["X"], (M, K))).to(cuda_device),
+                                     torch.from_numpy(arr(c["B"], (K, N))).to(cuda_device),
+                                     torch.from_numpy(arr(c["b"])).to(cuda_device), want_z=True)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32).ravel(), np.array(c["out"], np.uint32))
+    assert np.array_equal(z.cpu().numpy().view(np.uint32).ravel(), np.array(c["z"], np.uint32))
+    for ta in (0, 1):
+        for tb in (0, 1):
+            c = gold[f"matmul_ta{ta}_tb{tb}"]
+            A = torch.from_numpy(arr(c["A"], (K, M) if ta else (M, K))).to(cuda_device)
+            B = torch.from_numpy(arr(c["B"], (N, K) if tb else (K, N))).to(cuda_device)
+            got = exact.matmul(A, B, bool(ta), bool(tb)).cpu().numpy().view(np.uint32).ravel()
+            assert np.array_equal(got, np.array(c["out"], np.uint32))
