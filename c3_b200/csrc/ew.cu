@@ -35,12 +35,89 @@ constexpr int kRowsPerBlock = 512;  // rows one block reduces before the cross-b
 //         (reference: Mul(Gt(x, 0), grad), src/C3/C3BackwardCapture.cpp:501-528, where
 //         Gt yields 1.0f / 0.0f, src/C3/MLIRKernelGen.cpp:173-211).
 // !MASKED: input fp32, sum only (SumReduce axis 0, src/C3/C3DialectLowering.cpp:382-465).
+// Loads the 8 values a thread owns in row r (bf16 dY with its mask bits, or fp32).
+template <bool MASKED>
+__device__ __forceinline__ void colsum_load(const void* __restrict__ in, const uint32_t* __restrict__ mask,
+                                            int r, int col, int N, int ldm, bool vec, uint32_t (&raw)[8],
+                                            uint32_t& bits) {
+  if constexpr (MASKED) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in) + (int64_t)r * N + col;
+    if (vec) {
+      const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
+      raw[0] = q.x; raw[1] = q.y; raw[2] = q.z; raw[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t lo = (col + 2 * j < N) ? __bfloat16_as_ushort(src[2 * j]) : 0u;
+        const uint32_t hi = (col + 2 * j + 1 < N) ? __bfloat16_as_ushort(src[2 * j + 1]) : 0u;
+        raw[j] = lo | (hi << 16);
+      }
+    }
+    bits = __ldg(mask + (int64_t)r * ldm + (col >> 5)) >> (col & 31);
+  } else {
+    const float* src = static_cast<const float*>(in) + (int64_t)r * N + col;
+    if (vec) {
+      const uint4 a = __ldcs(reinterpret_cast<const uint4*>(src));
+      const uint4 b = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
+      raw[0] = a.x; raw[1] = a.y; raw[2] = a.z; raw[3] = a.w;
+      raw[4] = b.x; raw[5] = b.y; raw[6] = b.z; raw[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) raw[j] = (col + j < N) ? __float_as_uint(src[j]) : 0u;
+    }
+    bits = 0u;
+  }
+}
+
+// Processes row r from the loaded values: writes dZ (MASKED) and accumulates.
+template <bool MASKED>
+__device__ __forceinline__ void colsum_consume(__nv_bfloat16* __restrict__ dz, int r, int col, int N, bool vec,
+                                               const uint32_t (&raw)[8], uint32_t bits, float (&acc)[8]) {
+  float v[8];
+  if constexpr (MASKED) {
+    uint32_t outw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float g0 = __uint_as_float(raw[j] << 16);
+      const float g1 = __uint_as_float(raw[j] & 0xffff0000u);
+      v[2 * j] = __fmul_rn((bits >> (2 * j)) & 1u ? 1.f : 0.f, g0);
+      v[2 * j + 1] = __fmul_rn((bits >> (2 * j + 1)) & 1u ? 1.f : 0.f, g1);
+      // v is exactly g or a signed zero, so the bf16 repacking is exact.
+      outw[j] = (__float_as_uint(v[2 * j]) >> 16) | (__float_as_uint(v[2 * j + 1]) & 0xffff0000u);
+    }
+    __nv_bfloat16* dst = dz + (int64_t)r * N + col;
+    if (vec) {
+      __stcs(reinterpret_cast<uint4*>(dst), make_uint4(outw[0], outw[1], outw[2], outw[3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (col + j < N) dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(outw[j >> 1] >> (16 * (j & 1))));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+}
+
+// One block covers a strip of 256 columns and `rows_per_block` rows. Each thread owns 8
+// adjacent columns; warps stride over rows, four rows at a time with all loads issued
+// before any is consumed (memory-level parallelism). The block writes its 256 partial
+// sums to `partials[row_block][col]`; the last block of a strip to finish (atomic ticket)
+// adds the partials of that strip in row-block order, so the result does not depend on
+// scheduling.
+//
+// MASKED: input bf16 dY with a bit-packed mask; also writes dZ = float(bit) * dY as bf16
+//         (reference: Mul(Gt(x, 0), grad), src/C3/C3BackwardCapture.cpp:501-528, where
+//         Gt yields 1.0f / 0.0f, src/C3/MLIRKernelGen.cpp:173-211).
+// !MASKED: input fp32, sum only (SumReduce axis 0, src/C3/C3DialectLowering.cpp:382-465).
 template <bool MASKED>
 __global__ void __launch_bounds__(kWarps * 32)
     colsum_kernel(const void* __restrict__ in, const uint32_t* __restrict__ mask,
                   __nv_bfloat16* __restrict__ dz, float* __restrict__ out, int M, int N,
-                  int ldm, float* __restrict__ partials, unsigned int* __restrict__ tickets,
-                  int vec_ok) {
+                  int ldm, int rows_per_block, float* __restrict__ partials,
+                  unsigned int* __restrict__ tickets, int vec_ok) {
   __shared__ float red[kWarps][kColsPerWarp];
   __shared__ bool is_last;
   const int lane = threadIdx.x & 31;
@@ -48,8 +125,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int strip = blockIdx.x;
   const int rb = blockIdx.y;
   const int col = strip * kColsPerWarp + lane * 8;
-  const int row0 = rb * kRowsPerBlock;
-  const int row1 = min(M, row0 + kRowsPerBlock);
+  const int row0 = rb * rows_per_block;
+  const int row1 = min(M, row0 + rows_per_block);
 
   float acc[8];
 #pragma unroll
@@ -57,58 +134,18 @@ __global__ void __launch_bounds__(kWarps * 32)
 
   if (col < N) {
     const bool vec = vec_ok && (col + 8 <= N);
-#pragma unroll 4
-    for (int r = row0 + warp; r < row1; r += kWarps) {
-      float v[8];
-      if constexpr (MASKED) {
-        const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in) + (int64_t)r * N + col;
-        uint32_t raw[4];
-        if (vec) {
-          const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
-          raw[0] = q.x; raw[1] = q.y; raw[2] = q.z; raw[3] = q.w;
-        } else {
+    int r = row0 + warp;
+    for (; r + 3 * kWarps < row1; r += 4 * kWarps) {
+      uint32_t raw[4][8], bits[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t lo = (col + 2 * j < N) ? __bfloat16_as_ushort(src[2 * j]) : 0u;
-            const uint32_t hi = (col + 2 * j + 1 < N) ? __bfloat16_as_ushort(src[2 * j + 1]) : 0u;
-            raw[j] = lo | (hi << 16);
-          }
-        }
-        const uint32_t word = __ldg(mask + (int64_t)r * ldm + (col >> 5));
-        const uint32_t bits = word >> (col & 31);
-        uint32_t outw[4];
+      for (int u = 0; u < 4; ++u) colsum_load<MASKED>(in, mask, r + u * kWarps, col, N, ldm, vec, raw[u], bits[u]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float g0 = __uint_as_float(raw[j] << 16);
-          const float g1 = __uint_as_float(raw[j] & 0xffff0000u);
-          v[2 * j] = __fmul_rn((bits >> (2 * j)) & 1u ? 1.f : 0.f, g0);
-          v[2 * j + 1] = __fmul_rn((bits >> (2 * j + 1)) & 1u ? 1.f : 0.f, g1);
-          // v is exactly g or a signed zero, so the bf16 repacking is exact.
-          outw[j] = (__float_as_uint(v[2 * j]) >> 16) | (__float_as_uint(v[2 * j + 1]) & 0xffff0000u);
-        }
-        __nv_bfloat16* dst = dz + (int64_t)r * N + col;
-        if (vec) {
-          __stcs(reinterpret_cast<uint4*>(dst), make_uint4(outw[0], outw[1], outw[2], outw[3]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (col + j < N)
-              dst[j] = __ushort_as_bfloat16(static_cast<unsigned short>(outw[j >> 1] >> (16 * (j & 1))));
-        }
-      } else {
-        const float* src = static_cast<const float*>(in) + (int64_t)r * N + col;
-        if (vec) {
-          const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
-          const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
-          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] = (col + j < N) ? src[j] : 0.f;
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+      for (int u = 0; u < 4; ++u) colsum_consume<MASKED>(dz, r + u * kWarps, col, N, vec, raw[u], bits[u], acc);
+    }
+    for (; r < row1; r += kWarps) {
+      uint32_t raw[8], bits;
+      colsum_load<MASKED>(in, mask, r, col, N, ldm, vec, raw, bits);
+      colsum_consume<MASKED>(dz, r, col, N, vec, raw, bits, acc);
     }
   }
 
@@ -141,8 +178,20 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// Rows per block: enough blocks to fill the SMs several times over (at least 4 per SM),
+// between 64 and 512 rows, a multiple of the 8 warps x 4-row batches.
+int64_t colsum_rows_per_block(int64_t M, int64_t N) {
+  const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
+  const int64_t target_blocks = 4 * 148;
+  int64_t rows = (M * strips + target_blocks - 1) / target_blocks;
+  rows = (rows + 31) / 32 * 32;
+  if (rows < 64) rows = 64;
+  if (rows > kRowsPerBlock) rows = kRowsPerBlock;
+  return rows;
+}
+
 size_t colsum_workspace(int64_t M, int64_t N) {
-  const int64_t rbs = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int64_t rbs = (M + colsum_rows_per_block(M, N) - 1) / colsum_rows_per_block(M, N);
   const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
   const size_t partial_bytes = static_cast<size_t>(rbs > 0 ? rbs : 1) * static_cast<size_t>(N) * 4u;
   const size_t ticket_bytes = static_cast<size_t>(strips > 0 ? strips : 1) * 4u;
@@ -170,10 +219,11 @@ int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, in
     set_error("column sum: workspace of %zu bytes needed, %zu given", need, ws ? ws_bytes : 0);
     return C3CU_ERR_WORKSPACE;
   }
-  const int64_t rbs = (M + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int64_t rpb = colsum_rows_per_block(M, N);
+  const int64_t rbs = (M + rpb - 1) / rpb;
   const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
   if (rbs > 65535) {
-    set_error("column sum: M=%lld exceeds %lld rows", (long long)M, (long long)65535 * kRowsPerBlock);
+    set_error("column sum: M=%lld exceeds %lld rows", (long long)M, (long long)65535 * rpb);
     return C3CU_ERR_INVALID;
   }
   float* partials = static_cast<float*>(ws);
@@ -189,7 +239,7 @@ int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, in
   dim3 grid(static_cast<unsigned>(strips), static_cast<unsigned>(rbs));
   colsum_kernel<MASKED><<<grid, kWarps * 32, 0, st>>>(in, mask, static_cast<__nv_bfloat16*>(dz), out,
                                                      static_cast<int>(M), static_cast<int>(N), ldm,
-                                                     partials, tickets, vec_ok);
+                                                     static_cast<int>(rpb), partials, tickets, vec_ok);
   return cuda_status(cudaGetLastError(), "column sum: launch");
 }
 
@@ -205,11 +255,20 @@ __device__ __forceinline__ float chain_cfg4(float a, float b, float c) {
   return __fdiv_rn(r, d);
 }
 
+__device__ __forceinline__ float4 chain_cfg4_v(float4 a, float4 b, float4 c) {
+  return make_float4(chain_cfg4(a.x, b.x, c.x), chain_cfg4(a.y, b.y, c.y), chain_cfg4(a.z, b.z, c.z),
+                     chain_cfg4(a.w, b.w, c.w));
+}
+
+// Grid-stride over float4s; each iteration issues 4 float4 loads per input (12 x 16 B in
+// flight per thread) before computing, which keeps HBM busy at the measured copy bandwidth.
+constexpr int kCfg4Unroll = 4;
+
 __global__ void __launch_bounds__(256)
     chain_cfg4_kernel(const float* __restrict__ A, const float* __restrict__ B,
                       const float* __restrict__ C, float* __restrict__ out, int64_t n, int vec_ok) {
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t T = static_cast<int64_t>(gridDim.x) * blockDim.x;
   if (vec_ok) {
     const int64_t n4 = n >> 2;
     const float4* A4 = reinterpret_cast<const float4*>(A);
@@ -217,25 +276,21 @@ __global__ void __launch_bounds__(256)
     const float4* C4 = reinterpret_cast<const float4*>(C);
     float4* O4 = reinterpret_cast<float4*>(out);
     int64_t i = tid;
-    // two float4 per thread per iteration: 6 independent 16-byte loads in flight
-    for (; i + nthreads < n4; i += 2 * nthreads) {
-      const float4 a0 = __ldcs(A4 + i), b0 = __ldcs(B4 + i), c0 = __ldcs(C4 + i);
-      const float4 a1 = __ldcs(A4 + i + nthreads), b1 = __ldcs(B4 + i + nthreads),
-                   c1 = __ldcs(C4 + i + nthreads);
-      __stcs(O4 + i, make_float4(chain_cfg4(a0.x, b0.x, c0.x), chain_cfg4(a0.y, b0.y, c0.y),
-                                 chain_cfg4(a0.z, b0.z, c0.z), chain_cfg4(a0.w, b0.w, c0.w)));
-      __stcs(O4 + i + nthreads,
-             make_float4(chain_cfg4(a1.x, b1.x, c1.x), chain_cfg4(a1.y, b1.y, c1.y),
-                         chain_cfg4(a1.z, b1.z, c1.z), chain_cfg4(a1.w, b1.w, c1.w)));
+    for (; i + (kCfg4Unroll - 1) * T < n4; i += kCfg4Unroll * T) {
+      float4 a[kCfg4Unroll], b[kCfg4Unroll], c[kCfg4Unroll];
+#pragma unroll
+      for (int u = 0; u < kCfg4Unroll; ++u) {
+        a[u] = __ldcs(A4 + i + u * T);
+        b[u] = __ldcs(B4 + i + u * T);
+        c[u] = __ldcs(C4 + i + u * T);
+      }
+#pragma unroll
+      for (int u = 0; u < kCfg4Unroll; ++u) __stcs(O4 + i + u * T, chain_cfg4_v(a[u], b[u], c[u]));
     }
-    for (; i < n4; i += nthreads) {
-      const float4 a = __ldcs(A4 + i), b = __ldcs(B4 + i), c = __ldcs(C4 + i);
-      __stcs(O4 + i, make_float4(chain_cfg4(a.x, b.x, c.x), chain_cfg4(a.y, b.y, c.y),
-                                 chain_cfg4(a.z, b.z, c.z), chain_cfg4(a.w, b.w, c.w)));
-    }
-    for (int64_t k = (n4 << 2) + tid; k < n; k += nthreads) out[k] = chain_cfg4(A[k], B[k], C[k]);
+    for (; i < n4; i += T) __stcs(O4 + i, chain_cfg4_v(__ldcs(A4 + i), __ldcs(B4 + i), __ldcs(C4 + i)));
+    for (int64_t k = (n4 << 2) + tid; k < n; k += T) out[k] = chain_cfg4(A[k], B[k], C[k]);
   } else {
-    for (int64_t k = tid; k < n; k += nthreads) out[k] = chain_cfg4(A[k], B[k], C[k]);
+    for (int64_t k = tid; k < n; k += T) out[k] = chain_cfg4(A[k], B[k], C[k]);
   }
 }
 
@@ -329,10 +384,10 @@ __global__ void __launch_bounds__(256) bf16_to_f32_kernel(const __nv_bfloat16* _
     out[i] = __bfloat162float(in[i]);
 }
 
-int grid_for(int64_t work_items, int threads) {
+int grid_for(int64_t work_items, int threads, int blocks_per_sm = 8) {
   const int64_t sms = sm_count() > 0 ? sm_count() : 148;
   const int64_t want = (work_items + threads - 1) / threads;
-  const int64_t cap = sms * 8;  // 8 resident 256-thread blocks per SM
+  const int64_t cap = sms * blocks_per_sm;
   int64_t g = want < cap ? want : cap;
   return static_cast<int>(g > 0 ? g : 1);
 }
@@ -441,7 +496,7 @@ int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* ou
   }
   const int vec_ok = c3cu::aligned16(A) && c3cu::aligned16(B) && c3cu::aligned16(C) &&
                      c3cu::aligned16(out);
-  const int grid = c3cu::ew::grid_for((n + 7) / 8, 256);
+  const int grid = c3cu::ew::grid_for((n + 15) / 16, 256, 16);
   c3cu::ew::chain_cfg4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(A, B, C, out, n,
                                                                                    vec_ok);
   return c3cu::cuda_status(cudaGetLastError(), "ew_chain_cfg4: launch");
