@@ -2,7 +2,7 @@
 
     python -m c3_b200.profiling <case> [--iters N] [--m M] [--n N] [--k K] [--elems E]
 
-cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step
+cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step, attn
 Prints the CUDA-event time per launch and the algorithmic rate (TFLOP/s or GB/s)."""
 from __future__ import annotations
 
@@ -50,6 +50,14 @@ def _case(args, dev):
         C = torch.rand(n, generator=g, device=dev) * 8 - 4
         out = torch.empty_like(A)
         return (lambda: elementwise.chain_cfg4(A, B, C, out)), 16.0 * n, "GB/s"
+    if args.case == "attn":
+        from .attention import flash_attn_fwd
+        B, H, S = args.b, args.h, args.s
+        Q, K, V = [torch.randn((B, H, S, 128), generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+        O = torch.empty_like(Q)
+        L = torch.empty((B, H, S), device=dev)
+        flops = 2.0 * B * H * S * S * 128  # causal: half of 4 B H S^2 D
+        return (lambda: flash_attn_fwd(Q, K, V, True, None, O, L)), flops, "TFLOP/s"
     if args.case == "sum-rows":
         x = torch.randn((M, N), generator=g, device=dev)
         out = torch.empty(N, device=dev)
@@ -65,6 +73,9 @@ def main():
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--elems", type=int, default=1 << 28)
+    ap.add_argument("--b", type=int, default=8)
+    ap.add_argument("--h", type=int, default=32)
+    ap.add_argument("--s", type=int, default=8192)
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)

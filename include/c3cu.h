@@ -29,6 +29,9 @@
  *   c3cu_ew_program            <- FusedNode elementwise loops (src/C3/MLIRKernelGen.cpp:394-768) and
  *                                 LinalgFusedKernel (src/C3/LinalgFusedGen.cpp:141-378)
  *   c3cu_sum_rows_f32          <- SumReduceOpLowering axis 0 (src/C3/C3DialectLowering.cpp:382-465)
+ *   c3cu_flash_attn_fwd        <- no reference counterpart (the reference has no attention kernel;
+ *                                 op::Softmax exists only as a rolling-hash code,
+ *                                 src/C3/RollingHash.cpp:62)
  */
 #ifndef C3CU_H_
 #define C3CU_H_
@@ -175,6 +178,14 @@ int c3cu_convert(const void* in, int in_dtype, void* out, int out_dtype, int64_t
 size_t c3cu_sum_rows_f32_workspace(int64_t M, int64_t N);
 int c3cu_sum_rows_f32(const float* in, float* out, int64_t M, int64_t N, void* workspace,
                       size_t workspace_bytes, c3cu_stream_t stream);
+
+/* ------------------------------------------------------------------ attention
+ * FlashAttention forward: O = softmax(scale * Q K^T (+ causal mask)) V, bf16 in/out,
+ * fp32 accumulation; LSE[b][h][s] = natural-log sum of exp of the scaled, masked scores
+ * (may be NULL). Q, K, V, O: [B][H][S][D] contiguous bf16 with D = 128. */
+int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE,
+                        int64_t B, int64_t H, int64_t S, int64_t D, float scale, int causal,
+                        c3cu_stream_t stream);
 
 #ifdef __cplusplus
 }
