@@ -3,7 +3,7 @@
 // and LSE = log(sum exp(scale * Q K^T + mask)) (natural log) for bf16 Q, K, V of shape
 // [B, H, S, D=128] and fp32 LSE [B, H, S].
 //
-// One CTA per 128-row query tile (grid = B*H*ceil(S/128), heaviest causal tiles first):
+// One CTA per 128-row query tile (grid = B*H*ceil(S/128), head-major, heaviest tiles first):
 //   warp 0      TMA producer: Q once, then K_j / V_j (128 keys each) into a 2-stage ring
 //   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers
 //               (issued one block ahead, so it overlaps the softmax of the previous block),
@@ -55,6 +55,24 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed two-lane fp32 arithmetic (sm_100): halves the FMA-pipe instructions of the softmax.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
+
 __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
@@ -92,9 +110,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t warp = warp_id_sync();
   const uint32_t lane = lane_id();
 
-  // heaviest causal tiles first: block b -> query tile (q_tiles-1 - b / BH), head b % BH
-  const int bh = blockIdx.x % p.BH;
-  const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x / p.BH);
+  // Head-major order: the CTAs resident at one time share a few heads, so their K / V blocks
+  // are read from HBM once and then hit in L2; within a head the heaviest causal tiles
+  // (most key blocks) come first.
+  const int bh = static_cast<int>(blockIdx.x / p.q_tiles);
+  const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x % p.q_tiles);
   const int q0 = qt * BM;
   const int kv_blocks_total = (p.S + BN - 1) / BN;
   const int n = p.causal ? min(qt + 1, kv_blocks_total) : kv_blocks_total;
@@ -223,25 +243,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_ld();
       const int k0 = j * BN;
-      // scores in log2 units; masked keys (causal, or past the sequence end) get -inf
-      const bool edge = (p.causal && k0 + BN - 1 > row) || (k0 + BN > p.S);
-      float mx = -INFINITY;
+      // Masking (causal, or keys past the sequence end) only on edge blocks, outside the
+      // common path. The scale is positive, so the row maximum is taken on raw scores.
+      if ((p.causal && k0 + BN - 1 > row) || (k0 + BN > p.S)) {
+        const int lim = p.causal ? min(row, p.S - 1) : p.S - 1;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float v = s[i] * p.scale_log2;
-        if (edge) {
-          const int key = k0 + i;
-          if ((p.causal && key > row) || key >= p.S) v = -INFINITY;
-        }
-        s[i] = v;
-        mx = fmaxf(mx, v);
+        for (int i = 0; i < 128; ++i)
+          if (k0 + i > lim) s[i] = -INFINITY;
       }
-      const float m_new = fmaxf(m_used, mx);
+      float mx0 = s[0], mx1 = s[1];
+#pragma unroll
+      for (int i = 2; i < 128; i += 2) {
+        mx0 = fmaxf(mx0, s[i]);
+        mx1 = fmaxf(mx1, s[i + 1]);
+      }
+      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * p.scale_log2);
       const bool need = (m_used == -INFINITY) ? (m_new != -INFINITY) : (m_new > m_used + kRescaleThreshold);
       const float m_next = need ? m_new : m_used;
       const float alpha = need ? ((m_used == -INFINITY) ? 0.f : ex2(m_used - m_new)) : 1.f;
       const float base = (m_next == -INFINITY) ? 0.f : m_next;
-      float rs = 0.f;
+      // e = 2^(s * scale_log2 - base): one packed FMA per pair, then ex2
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 nb2 = make_float2(-base, -base);
+      float2 rs2 = make_float2(0.f, 0.f);
       // P_j (bf16, relative to m_next) overwrites the first 64 columns of this S buffer;
       // chunk c (keys 32c..32c+31) lands in columns 16c..16c+15, already read above.
 #pragma unroll
@@ -249,31 +273,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = ex2(s[c * 32 + 2 * i] - base), e1 = ex2(s[c * 32 + 2 * i + 1] - base);
-          rs += e0 + e1;
-          w[i] = pack_bf16x2(e0, e1);
+          float2 x = make_float2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
+          x = ffma2(x, sc2, nb2);
+          const float2 e = make_float2(ex2(x.x), ex2(x.y));
+          rs2 = fadd2(rs2, e);
+          w[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st_32x32b_x16(tmem + lane_base + s_col(j) + c * 16, w);
       }
+      const float rs = rs2.x + rs2.y;
       l = l * alpha + rs;
-      if (j > 0) {
-        // O may only be touched once PV_{j-1} has completed
+      // O may only be rescaled once PV_{j-1} has completed. P_j goes to the other S buffer
+      // and PV_j is issued after PV_{j-1} by the same thread (tcgen05.mma executes in issue
+      // order), so without a rescale the softmax does not wait for PV_{j-1}.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
         if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) / 2) & 1u, kFaultWaitAccFull)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            uint32_t lo[16], hi[16];
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          uint32_t lo[16], hi[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) { lo[i] = r[i]; hi[i] = r[16 + i]; }
-            tmem_st_32x32b_x16(tmem + lane_base + O_COL + c * 32, lo);
-            tmem_st_32x32b_x16(tmem + lane_base + O_COL + c * 32 + 16, hi);
-          }
+          for (int i = 0; i < 16; ++i) { lo[i] = r[i]; hi[i] = r[16 + i]; }
+          tmem_st_32x32b_x16(tmem + lane_base + O_COL + c * 32, lo);
+          tmem_st_32x32b_x16(tmem + lane_base + O_COL + c * 32 + 16, hi);
         }
       }
       m_used = m_next;

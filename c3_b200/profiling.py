@@ -96,7 +96,8 @@ def main():
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     print(json.dumps({"case": args.case, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
                       "ms_avg": avg, "ms_best": best, "rate_avg": work / (avg * 1e-3) / scale,
-                      "rate_best": work / (best * 1e-3) / scale, "unit": unit}))
+                      "rate_best": work / (best * 1e-3) / scale, "unit": unit,
+                      "times_ms": [round(t, 4) for t in times]}))
 
 
 if __name__ == "__main__":
