@@ -206,7 +206,7 @@ def run_c3(args):
                                 device_id=dev)
 
     import c3_b200
-    from c3_b200 import linear
+    from c3_b200 import _lib, linear
     L = c3_b200.load()
     c3_b200.device_check()
 
@@ -228,10 +228,20 @@ def run_c3(args):
 
     comp = torch.cuda.current_stream(dev)
     comm = torch.cuda.Stream(dev)
-    ev_dw_done = torch.cuda.Event()
     ev_ar_done = torch.cuda.Event()
     kinds = ("fwd", "prepass", "dw", "dx")
     kernel_events = {k: [] for k in kinds}
+    ar_events = []
+    # Data-parallel overlap: the dW GEMM runs in `chunks` row bands of dW; each band's
+    # all-reduce starts on the comm stream as soon as its GEMM ends (the last band carries
+    # db). `reserve` SMs are left to the collective while the dX GEMM overlaps it.
+    chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "2" if world > 1 else "1")))
+    reserve = int(os.environ.get("C3_BENCH_AR_SMS", "0")) if world > 1 else 0
+    if N % (chunks * 8) != 0:
+        chunks = 1
+    band = N // chunks
+    ev_band = [torch.cuda.Event() for _ in range(chunks)]
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def step(record: bool):
         evs = {}
@@ -242,19 +252,43 @@ def run_c3(args):
                 evs.setdefault(name, []).append(e)
         mark("fwd"); linear.forward(X, W, b, "nk", Y, mask); mark("fwd")
         mark("prepass"); linear.relu_mask_db(dY, mask, dZ, db); mark("prepass")
-        mark("dw"); linear.grad_weight(dZ, X, "nk", dW); mark("dw")
+        mark("dw")
+        ar = []
+        for c in range(chunks):
+            r0, r1 = c * band, (c + 1) * band
+            if chunks == 1:
+                linear.grad_weight(dZ, X, "nk", dW)
+            else:
+                linear.gemm(dZ[:, r0:r1], X, True, True, _lib.EPI_STORE_F32, dW[r0:r1],
+                            M=r1 - r0, N=K, K=M)
+            if world > 1:
+                ev_band[c].record(comp)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(ev_band[c])
+                    e0 = torch.cuda.Event(enable_timing=True) if record else None
+                    if record:
+                        e0.record(comm)
+                    lo, hi = r0 * K, (r1 * K if c < chunks - 1 else N * K + N)
+                    dist.all_reduce(grads[lo:hi])
+                    if record:
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e1.record(comm)
+                        ar.append((e0, e1))
+        mark("dw")
         if world > 1:
-            ev_dw_done.record(comp)
             with torch.cuda.stream(comm):
-                comm.wait_event(ev_dw_done)
-                dist.all_reduce(grads)
                 ev_ar_done.record(comm)
+        if reserve:
+            L.c3cu_set_gemm_max_ctas(sms - reserve)
         mark("dx"); linear.grad_input(dZ, W, "nk", dX); mark("dx")
+        if reserve:
+            L.c3cu_set_gemm_max_ctas(0)
         if world > 1:
             comp.wait_event(ev_ar_done)
         if record:
             for k in kinds:
                 kernel_events[k].append((evs[k][0], evs[k][1]))
+            ar_events.append(ar)
 
     for _ in range(max(args.warmup, 0)):
         step(False)
@@ -289,6 +323,8 @@ def run_c3(args):
 
     # per-kernel device time (this rank), for the roofline of the dominant kernel
     ktime = {k: sum(a.elapsed_time(bv) for a, bv in kernel_events[k]) / args.steps for k in kinds}
+    if world > 1:
+        ktime["allreduce"] = sum(a.elapsed_time(bv) for st in ar_events for a, bv in st) / args.steps
     gemm_ms = ktime["fwd"] + ktime["dw"] + ktime["dx"]
     gemm_flops = 3 * 2.0 * M * N * K
     peak_burst, peak_sust, hbm, peak_kind = _peaks()
@@ -313,7 +349,9 @@ def run_c3(args):
                        "N": N, "K": K, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (X, dY 128 MiB each at N=1)",
                        "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
-                               + (", NCCL all-reduce [dW|db] overlapped with dX" if world > 1 else "")},
+                               + (f", NCCL all-reduce of [dW|db] in {chunks} band(s), each started when its"
+                                  f" dW band ends, overlapped with the rest of dW and dX" if world > 1 else ""),
+                       "dw_bands": chunks, "sms_reserved_for_allreduce": reserve},
             "frac_of_peak": value / world / peak,
             "kernel_ms": ktime,
             "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",

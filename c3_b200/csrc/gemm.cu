@@ -1,5 +1,7 @@
 // C-ABI entry points of the tcgen05 GEMM family (include/c3cu.h): the fused
 // Linear+bias+ReLU forward, the dX / dW backward GEMMs and the general bf16 GEMM.
+#include <atomic>
+
 #include "gemm_tcgen05.cuh"
 #include "host_util.h"
 
@@ -9,6 +11,10 @@ namespace c3cu {
 namespace {
 
 using gemm::Params;
+
+// Upper bound on the persistent GEMM's CTAs (0 = one per SM). Lowering it leaves SMs free
+// for a collective that runs concurrently (e.g. an all-reduce overlapped with the dX GEMM).
+std::atomic<int> g_max_ctas{0};
 
 template <bool A_MN, bool B_MN, int EPI>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
@@ -38,7 +44,9 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
     attr_set = true;
   }
   const int tiles = ((p.M + gemm::BM - 1) / gemm::BM) * ((p.N + gemm::BN - 1) / gemm::BN);
-  const int sms = sm_count();
+  int sms = sm_count();
+  const int cap = g_max_ctas.load(std::memory_order_relaxed);
+  if (cap > 0 && cap < sms) sms = cap;
   const int grid = tiles < sms ? tiles : sms;
   kern<<<grid, gemm::kThreads, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
   return cuda_status(cudaGetLastError(), "gemm: launch");
@@ -119,6 +127,15 @@ int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ld
 }  // namespace c3cu
 
 extern "C" {
+
+int c3cu_set_gemm_max_ctas(int max_ctas) {
+  if (max_ctas < 0) {
+    c3cu::set_error("set_gemm_max_ctas: negative limit");
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::g_max_ctas.store(max_ctas, std::memory_order_relaxed);
+  return C3CU_OK;
+}
 
 int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
                    void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,

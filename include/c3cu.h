@@ -120,6 +120,10 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,
                    int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream);
 
+/* Library-wide cap on the CTAs of the persistent tensor-core GEMMs (0 = one per SM, the
+ * default). A host that overlaps a collective with a GEMM lowers it to leave SMs free. */
+int c3cu_set_gemm_max_ctas(int max_ctas);
+
 /* ------------------------------------------------------------------ exact fp32 (CUDA cores)
  * Bit-exact restatements of the reference's fp32 loops: every output element is reduced
  * over k in ascending order with separate round-to-nearest multiply and add.
