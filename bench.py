@@ -221,7 +221,20 @@ def run_c3(args):
     Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
     dZ = torch.empty_like(dY)
-    grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)  # packed [dW | db]
+    # packed [dW | db]; with N > 1 it lives in NVLink-multicast (symmetric) memory and is
+    # summed in the switch by the library's all-reduce kernel, unless C3_ALLREDUCE=nccl
+    collective = os.environ.get("C3_ALLREDUCE", "nvls") if world > 1 else "none"
+    nvls = None
+    if collective == "nvls":
+        try:
+            from c3_b200.collective import NvlsAllReduce
+            nvls = NvlsAllReduce(N * K + N, dev, num_ctas=int(os.environ.get("C3_NVLS_CTAS", "32")))
+            grads = nvls.data()
+        except Exception as exc:  # no multicast support: NCCL all-reduce instead
+            print(f"warning: NVLS all-reduce unavailable ({exc}); using NCCL", file=sys.stderr)
+            collective = "nccl"
+    if nvls is None:
+        grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
     dW = grads[: N * K].view(N, K)
     db = grads[N * K:]
     dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
@@ -269,7 +282,10 @@ def run_c3(args):
                     if record:
                         e0.record(comm)
                     lo, hi = r0 * K, (r1 * K if c < chunks - 1 else N * K + N)
-                    dist.all_reduce(grads[lo:hi])
+                    if nvls is not None:
+                        nvls.allreduce_(lo, hi, comm)
+                    else:
+                        dist.all_reduce(grads[lo:hi])
                     if record:
                         e1 = torch.cuda.Event(enable_timing=True)
                         e1.record(comm)
@@ -351,7 +367,10 @@ def run_c3(args):
                        "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
                                + (f", NCCL all-reduce of [dW|db] in {chunks} band(s), each started when its"
                                   f" dW band ends, overlapped with the rest of dW and dX" if world > 1 else ""),
-                       "dw_bands": chunks, "sms_reserved_for_allreduce": reserve},
+                       "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
+                       "allreduce": {"nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce_f32, "
+                                             "multimem.ld_reduce/st) on torch symmetric memory",
+                                     "nccl": "NCCL all_reduce", "none": "none"}[collective]},
             "frac_of_peak": value / world / peak,
             "kernel_ms": ktime,
             "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",
@@ -362,7 +381,7 @@ def run_c3(args):
                          "frac_of_sustained": achieved / peak_sust,
                          "frac_of_spec_2250": achieved / 2250.0,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": (4 + (chunks - 1) + (chunks if nvls is not None else 0)) * args.steps,
             "clocks": sampler.record(),
         }
         if e2e is not None:

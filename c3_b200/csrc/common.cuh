@@ -32,6 +32,7 @@ enum FaultCode : uint32_t {
   kFaultDrain = 5,          // drain after a fault itself timed out
   kFaultWaitSoftmax = 6,    // attention: softmax/correction handshake timed out
   kFaultBounds = 7,         // a debug bounds predicate fired (access skipped)
+  kFaultWaitPeer = 8,       // collective: another rank did not reach a barrier in time
 };
 
 }  // namespace c3cu

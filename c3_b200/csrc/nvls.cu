@@ -1,0 +1,138 @@
+// In-switch (NVLink SHARP) all-reduce of an fp32 buffer held in multicast-mapped memory.
+//
+// Every rank's buffer is bound to one NVLink multicast object. Rank r owns slice r of the
+// buffer: it loads that slice through the multicast address with multimem.ld_reduce (the
+// NVSwitch returns the sum over all ranks) and writes the sum back with multimem.st (the
+// switch writes it into every rank's copy). Per rank, one buffer's worth of data crosses
+// NVLink in each direction, and the reduction itself costs no SM arithmetic.
+//
+// Ordering: a rank may read peers' data only after every peer has finished writing it, and
+// the result may be consumed only after every rank has stored its slice. Both points are
+// grid-wide, cross-GPU barriers on a counter that lives in the same multicast buffer:
+// multimem.red.release adds 1 to every rank's copy of the counter, and each CTA spins
+// (bounded by %globaltimer) with acquire loads on its local copy until all ranks have
+// arrived. The counter only grows: call e (0-based, the same on every rank) waits for
+// world * (2e + 1) and world * (2e + 2).
+//
+// No TMA and no multicast TMA loads are used; only multimem loads/stores/reductions.
+#include "common.cuh"
+#include "host_util.h"
+
+C3CU_FAULT_ACCESSORS(nvls)
+
+namespace c3cu {
+namespace nvls {
+
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ void mm_ld_reduce_v4(const float* mc, float4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+}
+
+__device__ __forceinline__ void mm_st_v4(float* mc, const float4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void mm_ld_reduce(const float* mc, float& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(mc) : "memory");
+}
+
+__device__ __forceinline__ void mm_st(float* mc, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void mm_red_release_add(uint32_t* mc, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide cross-rank barrier: every CTA adds 1 through the multicast address, then waits
+// until all world * gridDim.x arrivals of this phase are visible in the local copy.
+__device__ bool barrier(uint32_t* mc_flag, const uint32_t* local_flag, uint32_t target) {
+  __syncthreads();
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    mm_red_release_add(mc_flag, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    while (static_cast<int32_t>(ld_acquire_sys(local_flag) - target) < 0) {
+      if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS / 2) {
+        record_fault(kFaultWaitPeer, blockIdx.x & 0xffffu);
+        ok = false;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+
+__global__ void __launch_bounds__(kThreads)
+    allreduce_kernel(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag, int64_t lo,
+                     int64_t hi, int rank, int world, uint32_t epoch) {
+  const uint32_t arrivals = static_cast<uint32_t>(world) * gridDim.x;
+  if (!barrier(mc_flag, local_flag, arrivals * (2u * epoch + 1u))) return;
+  // slice of [lo, hi) owned by this rank, in float4 units where aligned
+  const int64_t n = hi - lo;
+  const int64_t per = ((n + world - 1) / world + 3) / 4 * 4;
+  const int64_t s0 = lo + per * rank;
+  const int64_t s1 = min(hi, s0 + per);
+  if (s0 < s1) {
+    const int64_t v0 = (s0 + 3) / 4 * 4;
+    const int64_t v1 = s1 / 4 * 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (v0 < v1) {
+      for (int64_t i = v0 + 4 * t; i < v1; i += 4 * stride) {
+        float4 v;
+        mm_ld_reduce_v4(mc_data + i, v);
+        mm_st_v4(mc_data + i, v);
+      }
+    }
+    // unaligned head and tail of the slice
+    for (int64_t i = s0 + t; i < min(v0, s1); i += stride) {
+      float v;
+      mm_ld_reduce(mc_data + i, v);
+      mm_st(mc_data + i, v);
+    }
+    for (int64_t i = max(v1, v0) + t; i < s1; i += stride) {
+      float v;
+      mm_ld_reduce(mc_data + i, v);
+      mm_st(mc_data + i, v);
+    }
+  }
+  barrier(mc_flag, local_flag, arrivals * (2u * epoch + 2u));
+}
+
+}  // namespace nvls
+}  // namespace c3cu
+
+extern "C" int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,
+                                       int64_t lo, int64_t hi, int rank, int world, uint32_t epoch,
+                                       int num_ctas, c3cu_stream_t stream) {
+  using namespace c3cu;
+  int rc = require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (!mc_data || !mc_flag || !local_flag || lo < 0 || hi < lo || world < 1 || rank < 0 ||
+      rank >= world || num_ctas < 1 || num_ctas > 1024) {
+    set_error("nvls_allreduce_f32: bad arguments");
+    return C3CU_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(mc_data) & 15u) != 0u) {
+    set_error("nvls_allreduce_f32: multicast base must be 16-byte aligned");
+    return C3CU_ERR_ALIGN;
+  }
+  nvls::allreduce_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      mc_data, mc_flag, local_flag, lo, hi, rank, world, epoch);
+  return cuda_status(cudaGetLastError(), "nvls_allreduce_f32: launch");
+}

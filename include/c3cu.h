@@ -191,6 +191,19 @@ int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, fl
                         int64_t B, int64_t H, int64_t S, int64_t D, float scale, int causal,
                         c3cu_stream_t stream);
 
+/* ------------------------------------------------------------------ data-parallel collective
+ * In-switch (NVLink SHARP) all-reduce (sum) of fp32 elements [lo, hi) of a buffer that every
+ * rank has bound to one NVLink multicast object. mc_data / mc_flag are the multicast
+ * addresses of the data and of a uint32 barrier counter in the same buffer, local_flag
+ * this rank's own copy of that counter (zero on every rank before the first call). Every
+ * rank calls with the same lo, hi, num_ctas and epoch (0, 1, 2, ... per call). Waits on
+ * peers are bounded; a rank that never arrives makes the kernel record a fault
+ * (c3cu_fault_status) and return. The dW/db all-reduce of the data-parallel training step
+ * uses it; the reference has no collective. */
+int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,
+                            int64_t lo, int64_t hi, int rank, int world, uint32_t epoch,
+                            int num_ctas, c3cu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
