@@ -26,19 +26,25 @@ class NvlsAllReduce:
         self.num_ctas = num_ctas
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
-        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
-        if enable is not None:
-            try:
-                enable(self.group.group_name)
-            except Exception:  # already enabled / not needed in this torch version
-                pass
         self.buf = symm_mem.empty(numel + _FLAG_PAD, dtype=torch.float32, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
         self.hdl = symm_mem.rendezvous(self.buf, self.group)
-        self.mc = int(self.hdl.multicast_ptr)
-        if self.mc == 0:
+        mc_base = int(self.hdl.multicast_ptr)
+        if mc_base == 0:
             raise RuntimeError("NVLink multicast is not available for this process group")
+        # The handle describes the whole symmetric allocation; this tensor sits `offset`
+        # bytes into it (the same offset on every rank and in the multicast mapping).
+        offset = int(getattr(self.hdl, "offset", 0))
+        local_base = int(self.hdl.buffer_ptrs[self.rank])
+        if offset == 0 and local_base != self.buf.data_ptr():
+            offset = self.buf.data_ptr() - local_base
+        if local_base + offset != self.buf.data_ptr():
+            raise RuntimeError("symmetric buffer pointers are inconsistent "
+                               f"(base {local_base:#x} + offset {offset} != {self.buf.data_ptr():#x})")
+        if int(self.hdl.buffer_size) < offset + (numel + _FLAG_PAD) * 4:
+            raise RuntimeError("symmetric allocation smaller than the gradient buffer")
+        self.mc = mc_base + offset
         self.flag_local = self.buf.data_ptr() + numel * 4
         self.flag_mc = self.mc + numel * 4
         self.epoch = 0

@@ -1,0 +1,72 @@
+"""Data-parallel path on 2 GPUs (child processes, one per GPU): the in-switch all-reduce kernel
+against NCCL's all_reduce on the same buffers, and the row-sharded training step against the
+one-GPU step on the full batch. Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        import c3_b200
+        from c3_b200.collective import NvlsAllReduce
+        n = 1 << 20
+        ar = NvlsAllReduce(n + 7, dev, num_ctas=8)
+        results = {}
+        for trial in range(3):
+            g = torch.Generator(device=dev).manual_seed(100 * trial + rank)
+            x = torch.randn(n + 7, generator=g, device=dev)
+            ar.data().copy_(x)
+            ref = x.clone()
+            dist.all_reduce(ref)
+            # two calls per trial: a partial range, then the rest
+            ar.allreduce_(0, 3000)
+            ar.allreduce_(3000, n + 7)
+            torch.cuda.synchronize()
+            results[trial] = float((ar.data() - ref).abs().max() / ref.abs().max())
+        c3_b200.fault_status()
+        q.put((rank, "ok", results))
+        dist.barrier()
+        del ar
+        dist.destroy_process_group()
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc)))
+
+
+def test_nvls_allreduce_matches_nccl(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, res in out:
+        assert status == "ok", f"rank {rank}: {res}"
+        # fp32 sums of two values: the switch and NCCL may round in a different order
+        assert all(v <= 1e-6 for v in res.values()), res
