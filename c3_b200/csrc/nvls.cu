@@ -24,6 +24,7 @@ namespace c3cu {
 namespace nvls {
 
 constexpr int kThreads = 512;
+constexpr int kUnroll = 8;
 
 __device__ __forceinline__ void mm_ld_reduce_v4(const float* mc, float4& v) {
   asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -93,7 +94,17 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (v0 < v1) {
-      for (int64_t i = v0 + 4 * t; i < v1; i += 4 * stride) {
+      // kUnroll switch round trips in flight per thread: multimem.ld_reduce has a long
+      // latency (the switch gathers from every GPU), so throughput needs many outstanding.
+      int64_t i = v0 + 4 * t;
+      for (; i + 4 * stride * (kUnroll - 1) < v1; i += 4 * stride * kUnroll) {
+        float4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) mm_ld_reduce_v4(mc_data + i + 4 * stride * u, v[u]);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) mm_st_v4(mc_data + i + 4 * stride * u, v[u]);
+      }
+      for (; i < v1; i += 4 * stride) {
         float4 v;
         mm_ld_reduce_v4(mc_data + i, v);
         mm_st_v4(mc_data + i, v);
