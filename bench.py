@@ -221,22 +221,36 @@ def run_c3(args):
     Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
     dZ = torch.empty_like(dY)
-    # packed [dW | db]; with N > 1 it lives in NVLink-multicast (symmetric) memory and is
-    # summed in the switch by the library's all-reduce kernel, unless C3_ALLREDUCE=nccl
+    # Gradients: dW in bf16 (fp32 accumulation in the GEMM, one rounding) and db in fp32 by
+    # default; C3_GRAD_DTYPE=fp32 keeps dW in fp32. With N > 1 both live in NVLink-multicast
+    # (symmetric) memory and are summed in the switch by the library's all-reduce kernel
+    # (fp32 accumulation for bf16), unless C3_ALLREDUCE=nccl.
+    grad_bf16 = os.environ.get("C3_GRAD_DTYPE", "bf16") == "bf16"
     collective = os.environ.get("C3_ALLREDUCE", "nvls") if world > 1 else "none"
     nvls = None
     if collective == "nvls":
         try:
             from c3_b200.collective import NvlsAllReduce
-            nvls = NvlsAllReduce(N * K + N, dev, num_ctas=int(os.environ.get("C3_NVLS_CTAS", "32")))
-            grads = nvls.data()
+            ctas = int(os.environ.get("C3_NVLS_CTAS", "16"))
+            if grad_bf16:
+                nvls = NvlsAllReduce(N, dev, num_ctas=ctas, numel_bf16=N * K)
+                dW, db = nvls.bf16.view(N, K), nvls.f32
+            else:
+                nvls = NvlsAllReduce(N * K + N, dev, num_ctas=ctas)
+                grads = nvls.data()
+                dW, db = grads[: N * K].view(N, K), grads[N * K:]
         except Exception as exc:  # no multicast support: NCCL all-reduce instead
             print(f"warning: NVLS all-reduce unavailable ({exc}); using NCCL", file=sys.stderr)
             collective = "nccl"
+            nvls = None
     if nvls is None:
-        grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
-    dW = grads[: N * K].view(N, K)
-    db = grads[N * K:]
+        if grad_bf16:
+            dW = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
+            db = torch.empty(N, dtype=torch.float32, device=dev)
+        else:
+            grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
+            dW, db = grads[: N * K].view(N, K), grads[N * K:]
+    dW_epi = _lib.EPI_STORE_BF16 if grad_bf16 else _lib.EPI_STORE_F32
     dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
 
     comp = torch.cuda.current_stream(dev)
@@ -269,11 +283,7 @@ def run_c3(args):
         ar = []
         for c in range(chunks):
             r0, r1 = c * band, (c + 1) * band
-            if chunks == 1:
-                linear.grad_weight(dZ, X, "nk", dW)
-            else:
-                linear.gemm(dZ[:, r0:r1], X, True, True, _lib.EPI_STORE_F32, dW[r0:r1],
-                            M=r1 - r0, N=K, K=M)
+            linear.gemm(dZ[:, r0:r1], X, True, True, dW_epi, dW[r0:r1], M=r1 - r0, N=K, K=M)
             if world > 1:
                 ev_band[c].record(comp)
                 with torch.cuda.stream(comm):
@@ -281,11 +291,17 @@ def run_c3(args):
                     e0 = torch.cuda.Event(enable_timing=True) if record else None
                     if record:
                         e0.record(comm)
-                    lo, hi = r0 * K, (r1 * K if c < chunks - 1 else N * K + N)
-                    if nvls is not None:
-                        nvls.allreduce_(lo, hi, comm)
+                    last = c == chunks - 1
+                    if nvls is not None and grad_bf16:
+                        nvls.allreduce2_((r0 * K, r1 * K), (0, N) if last else None, comm)
+                    elif nvls is not None:
+                        nvls.allreduce_(r0 * K, r1 * K if not last else N * K + N, comm)
+                    elif grad_bf16:
+                        dist.all_reduce(dW[r0:r1])
+                        if last:
+                            dist.all_reduce(db)
                     else:
-                        dist.all_reduce(grads[lo:hi])
+                        dist.all_reduce(grads[r0 * K:(r1 * K if not last else N * K + N)])
                     if record:
                         e1 = torch.cuda.Event(enable_timing=True)
                         e1.record(comm)
@@ -365,10 +381,11 @@ def run_c3(args):
                        "N": N, "K": K, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (X, dY 128 MiB each at N=1)",
                        "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
-                               + (f", NCCL all-reduce of [dW|db] in {chunks} band(s), each started when its"
+                               + (f", all-reduce of dW and db in {chunks} band(s), each started when its"
                                   f" dW band ends, overlapped with the rest of dW and dX" if world > 1 else ""),
+                       "grad_dtype": {"dW": "bf16" if grad_bf16 else "fp32", "db": "fp32"},
                        "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
-                       "allreduce": {"nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce_f32, "
+                       "allreduce": {"nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce, "
                                              "multimem.ld_reduce/st) on torch symmetric memory",
                                      "nccl": "NCCL all_reduce", "none": "none"}[collective]},
             "frac_of_peak": value / world / peak,
@@ -409,18 +426,19 @@ def run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L):
     hb = torch.empty((N,), dtype=torch.float32, pin_memory=True); hb.copy_(b)
     hY = torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True)
     hdX = torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True)
-    hgrads = torch.empty(N * K + N, dtype=torch.float32, pin_memory=True)
+    grad_bf16 = os.environ.get("C3_GRAD_DTYPE", "bf16") == "bf16"
+    hdW = torch.empty((N, K), dtype=torch.bfloat16 if grad_bf16 else torch.float32, pin_memory=True)
+    hdb = torch.empty(N, dtype=torch.float32, pin_memory=True)
     dXd, dWd = torch.empty_like(X), torch.empty_like(W)
     Xd, dYd, bd = torch.empty_like(X), torch.empty_like(dY), torch.empty_like(b)
     Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
     dZ = torch.empty_like(dY)
-    grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
-    dW = grads[: N * K].view(N, K)
-    db = grads[N * K:]
+    dW = torch.empty((N, K), dtype=hdW.dtype, device=dev)
+    db = torch.empty(N, dtype=torch.float32, device=dev)
     dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
     h2d = hX.numel() * 2 + hdY.numel() * 2 + hW.numel() * 2 + hb.numel() * 4
-    d2h = hY.numel() * 2 + hdX.numel() * 2 + hgrads.numel() * 4
+    d2h = hY.numel() * 2 + hdX.numel() * 2 + hdW.numel() * hdW.element_size() + hdb.numel() * 4
 
     def step():
         Xd.copy_(hX, non_blocking=True); dWd.copy_(hW, non_blocking=True)
@@ -431,10 +449,12 @@ def run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L):
         linear.relu_mask_db(dYd, mask, dZ, db)
         linear.grad_weight(dZ, Xd, "nk", dW)
         if world > 1:
-            dist.all_reduce(grads)
+            dist.all_reduce(dW)
+            dist.all_reduce(db)
         linear.grad_input(dZ, dWd, "nk", dX)
         hdX.copy_(dX, non_blocking=True)
-        hgrads.copy_(grads, non_blocking=True)
+        hdW.copy_(dW, non_blocking=True)
+        hdb.copy_(db, non_blocking=True)
 
     for _ in range(max(args.warmup, 1)):
         step()

@@ -1,10 +1,12 @@
 """Gradient all-reduce of the data-parallel training step over NVLink.
 
-NvlsAllReduce keeps an fp32 buffer (the packed [dW | db] gradients) in torch symmetric
-memory, which binds every rank's copy to one NVLink multicast object, and sums it with the
-library's in-switch all-reduce kernel (c3cu_nvls_allreduce_f32): each rank reduces its slice
-through multimem.ld_reduce and broadcasts it with multimem.st. torch provides the allocation
-and the multicast mapping (plumbing); the reduction is this library's kernel.
+NvlsAllReduce keeps the gradient buffer in torch symmetric memory, which binds every rank's
+copy to one NVLink multicast object, and sums it with the library's in-switch all-reduce
+kernels (c3cu_nvls_allreduce, c3cu_nvls_allreduce_f32): each rank reduces its slice through
+multimem.ld_reduce and broadcasts it with multimem.st. The buffer has a bf16 region (e.g. dW,
+summed with fp32 accumulation in the switch) and an fp32 region (e.g. db, or an fp32 dW).
+torch provides the allocation and the multicast mapping (plumbing); the reduction is this
+library's kernel.
 """
 from __future__ import annotations
 
@@ -15,18 +17,27 @@ import torch.distributed as dist
 
 from . import _lib
 
-_FLAG_PAD = 64  # floats after the data: one uint32 barrier counter on its own 256 B
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
 
 
 class NvlsAllReduce:
-    def __init__(self, numel: int, device: torch.device, group=None, num_ctas: int = 32):
+    def __init__(self, numel: int, device: torch.device, group=None, num_ctas: int = 32,
+                 numel_bf16: int = 0):
+        """numel fp32 elements (region `f32`) and numel_bf16 bf16 elements (region `bf16`)."""
         import torch.distributed._symmetric_memory as symm_mem
         self.group = group or dist.group.WORLD
         self.numel = numel
+        self.numel_bf16 = numel_bf16
         self.num_ctas = num_ctas
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
-        self.buf = symm_mem.empty(numel + _FLAG_PAD, dtype=torch.float32, device=device)
+        self.bf16_off = 0
+        self.f32_off = _align(numel_bf16 * 2)
+        self.flag_off = _align(self.f32_off + numel * 4)
+        nbytes = self.flag_off + 256
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
         self.hdl = symm_mem.rendezvous(self.buf, self.group)
@@ -42,24 +53,43 @@ class NvlsAllReduce:
         if local_base + offset != self.buf.data_ptr():
             raise RuntimeError("symmetric buffer pointers are inconsistent "
                                f"(base {local_base:#x} + offset {offset} != {self.buf.data_ptr():#x})")
-        if int(self.hdl.buffer_size) < offset + (numel + _FLAG_PAD) * 4:
+        if int(self.hdl.buffer_size) < offset + nbytes:
             raise RuntimeError("symmetric allocation smaller than the gradient buffer")
         self.mc = mc_base + offset
-        self.flag_local = self.buf.data_ptr() + numel * 4
-        self.flag_mc = self.mc + numel * 4
+        self.flag_local = self.buf.data_ptr() + self.flag_off
+        self.flag_mc = self.mc + self.flag_off
+        self.f32 = self.buf[self.f32_off:self.f32_off + numel * 4].view(torch.float32)
+        self.bf16 = self.buf[self.bf16_off:self.bf16_off + numel_bf16 * 2].view(torch.bfloat16)
         self.epoch = 0
         dist.barrier(group=self.group)
         torch.cuda.synchronize(device)
 
     def data(self) -> torch.Tensor:
-        return self.buf[: self.numel]
+        """The fp32 region."""
+        return self.f32
 
     def allreduce_(self, lo: int = 0, hi: int | None = None, stream: torch.cuda.Stream | None = None):
+        """Sum fp32 elements [lo, hi) of the fp32 region over all ranks (any alignment)."""
         hi = self.numel if hi is None else hi
         s = stream or torch.cuda.current_stream(self.buf.device)
-        rc = _lib.load().c3cu_nvls_allreduce_f32(ctypes.c_void_p(self.mc), ctypes.c_void_p(self.flag_mc),
+        rc = _lib.load().c3cu_nvls_allreduce_f32(ctypes.c_void_p(self.mc + self.f32_off),
+                                                 ctypes.c_void_p(self.flag_mc),
                                                  ctypes.c_void_p(self.flag_local), lo, hi, self.rank,
                                                  self.world, self.epoch, self.num_ctas,
                                                  ctypes.c_void_p(s.cuda_stream))
         _lib.check(rc, "c3cu_nvls_allreduce_f32")
+        self.epoch += 1
+
+    def allreduce2_(self, bf16_range=None, f32_range=None, stream: torch.cuda.Stream | None = None):
+        """One call summing bf16 elements [lo, hi) (lo, hi multiples of 8) and fp32 elements
+        [lo, hi) (multiples of 4) of the two regions."""
+        blo, bhi = bf16_range or (0, 0)
+        flo, fhi = f32_range or (0, 0)
+        s = stream or torch.cuda.current_stream(self.buf.device)
+        rc = _lib.load().c3cu_nvls_allreduce(ctypes.c_void_p(self.mc), ctypes.c_void_p(self.flag_mc),
+                                             ctypes.c_void_p(self.flag_local), self.bf16_off + 2 * blo,
+                                             bhi - blo, self.f32_off + 4 * flo, fhi - flo, self.rank,
+                                             self.world, self.epoch, self.num_ctas,
+                                             ctypes.c_void_p(s.cuda_stream))
+        _lib.check(rc, "c3cu_nvls_allreduce")
         self.epoch += 1

@@ -61,6 +61,7 @@ int dispatch(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, i
   C3CU_GEMM_CASE(0, 0, kEpiStoreBf16)
   C3CU_GEMM_CASE(0, 1, kEpiStoreBf16)
   C3CU_GEMM_CASE(1, 1, kEpiStoreF32)
+  C3CU_GEMM_CASE(1, 1, kEpiStoreBf16)
   C3CU_GEMM_CASE(0, 0, kEpiStoreF32)
   C3CU_GEMM_CASE(0, 1, kEpiStoreF32)
   C3CU_GEMM_CASE(1, 0, kEpiStoreF32)

@@ -78,6 +78,80 @@ __device__ bool barrier(uint32_t* mc_flag, const uint32_t* local_flag, uint32_t 
   return __syncthreads_and(ok ? 1 : 0) != 0;
 }
 
+__device__ __forceinline__ void mm_ld_reduce_bf16x8(const void* mc, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+}
+
+__device__ __forceinline__ void mm_st_bf16x8(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Reduces this rank's slice of a segment of `count` elements at `mc` (16-byte units of
+// kPerVec elements; count must be a multiple of kPerVec).
+template <bool BF16>
+__device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int rank, int world) {
+  constexpr int64_t kPerVec = BF16 ? 8 : 4;
+  const int64_t nvec = count / kPerVec;
+  const int64_t per = (nvec + world - 1) / world;
+  const int64_t v0 = per * rank;
+  const int64_t v1 = min(nvec, v0 + per);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = v0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + stride * (kUnroll - 1) < v1; i += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint8_t* a = mc + (i + stride * u) * 16;
+      if (BF16) {
+        mm_ld_reduce_bf16x8(a, v[u]);
+      } else {
+        float4 f;
+        mm_ld_reduce_v4(reinterpret_cast<float*>(a), f);
+        v[u] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint8_t* a = mc + (i + stride * u) * 16;
+      if (BF16)
+        mm_st_bf16x8(a, v[u]);
+      else
+        mm_st_v4(reinterpret_cast<float*>(a), make_float4(__uint_as_float(v[u].x), __uint_as_float(v[u].y),
+                                                          __uint_as_float(v[u].z), __uint_as_float(v[u].w)));
+    }
+  }
+  for (; i < v1; i += stride) {
+    uint8_t* a = mc + i * 16;
+    if (BF16) {
+      uint4 v;
+      mm_ld_reduce_bf16x8(a, v);
+      mm_st_bf16x8(a, v);
+    } else {
+      float4 f;
+      mm_ld_reduce_v4(reinterpret_cast<float*>(a), f);
+      mm_st_v4(reinterpret_cast<float*>(a), f);
+    }
+  }
+}
+
+// One call: a bf16 segment and an fp32 segment of the same multicast buffer, between the
+// two cross-rank barriers.
+__global__ void __launch_bounds__(kThreads)
+    allreduce2_kernel(uint8_t* mc_base, uint32_t* mc_flag, const uint32_t* local_flag, int64_t bf16_off,
+                      int64_t bf16_count, int64_t f32_off, int64_t f32_count, int rank, int world,
+                      uint32_t epoch) {
+  const uint32_t arrivals = static_cast<uint32_t>(world) * gridDim.x;
+  if (!barrier(mc_flag, local_flag, arrivals * (2u * epoch + 1u))) return;
+  if (bf16_count > 0) reduce_segment<true>(mc_base + bf16_off, bf16_count, rank, world);
+  if (f32_count > 0) reduce_segment<false>(mc_base + f32_off, f32_count, rank, world);
+  barrier(mc_flag, local_flag, arrivals * (2u * epoch + 2u));
+}
+
 __global__ void __launch_bounds__(kThreads)
     allreduce_kernel(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag, int64_t lo,
                      int64_t hi, int rank, int world, uint32_t epoch) {
@@ -127,6 +201,30 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace nvls
 }  // namespace c3cu
+
+extern "C" int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint32_t* local_flag,
+                                   int64_t bf16_offset, int64_t bf16_count, int64_t f32_offset,
+                                   int64_t f32_count, int rank, int world, uint32_t epoch, int num_ctas,
+                                   c3cu_stream_t stream) {
+  using namespace c3cu;
+  int rc = require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (!mc_base || !mc_flag || !local_flag || bf16_offset < 0 || bf16_count < 0 || f32_offset < 0 ||
+      f32_count < 0 || world < 1 || rank < 0 || rank >= world || num_ctas < 1 || num_ctas > 1024) {
+    set_error("nvls_allreduce: bad arguments");
+    return C3CU_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(mc_base) & 15u) || (bf16_offset & 15) || (f32_offset & 15) ||
+      (bf16_count % 8) || (f32_count % 4)) {
+    set_error("nvls_allreduce: segments must start on 16 bytes and hold whole 16-byte vectors "
+              "(bf16 count %% 8, fp32 count %% 4)");
+    return C3CU_ERR_ALIGN;
+  }
+  nvls::allreduce2_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(mc_base), mc_flag, local_flag, bf16_offset, bf16_count, f32_offset, f32_count,
+      rank, world, epoch);
+  return cuda_status(cudaGetLastError(), "nvls_allreduce: launch");
+}
 
 extern "C" int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,
                                        int64_t lo, int64_t hi, int rank, int world, uint32_t epoch,

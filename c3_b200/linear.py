@@ -109,15 +109,22 @@ def grad_input(dZ: torch.Tensor, W: torch.Tensor, w_layout: str = "nk", dX: torc
     return dX
 
 
-def grad_weight(dZ: torch.Tensor, X: torch.Tensor, w_layout: str = "nk", dW: torch.Tensor | None = None):
+def grad_weight(dZ: torch.Tensor, X: torch.Tensor, w_layout: str = "nk", dW: torch.Tensor | None = None,
+                out_dtype: torch.dtype = torch.float32):
+    """dW = dZ^T X ([N, K], "nk") or X^T dZ ([K, N], "kn"), fp32 or bf16 (fp32 accumulation)."""
     lay = _layout(w_layout)
     _require(dZ, "dZ", torch.bfloat16, 2)
     _require(X, "X", torch.bfloat16, 2)
     M, N = dZ.shape
     K = X.shape[1]
     shape = (N, K) if lay == _lib.W_NK else (K, N)
+    if dW is not None:
+        out_dtype = dW.dtype
     if dW is None:
-        dW = torch.empty(shape, dtype=torch.float32, device=dZ.device)
+        dW = torch.empty(shape, dtype=out_dtype, device=dZ.device)
+    if out_dtype == torch.bfloat16:
+        A, B = (dZ, X) if lay == _lib.W_NK else (X, dZ)
+        return gemm(A, B, True, True, _lib.EPI_STORE_BF16, dW, M=shape[0], N=shape[1], K=M)
     rc = _lib.load().c3cu_gemm_dw(_p(dZ), _p(X), _p(dW), M, N, K, lay, _stream(dZ.device))
     _lib.check(rc, "c3cu_gemm_dw")
     return dW

@@ -203,6 +203,13 @@ int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, fl
 int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,
                             int64_t lo, int64_t hi, int rank, int world, uint32_t epoch,
                             int num_ctas, c3cu_stream_t stream);
+/* The same protocol over two segments of one multicast buffer in one call: bf16_count bf16
+ * elements at byte offset bf16_offset (summed in the switch with fp32 accumulation, one
+ * rounding to bf16) and f32_count fp32 elements at f32_offset. Offsets are multiples of 16
+ * bytes, bf16_count of 8 and f32_count of 4. */
+int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint32_t* local_flag,
+                        int64_t bf16_offset, int64_t bf16_count, int64_t f32_offset, int64_t f32_count,
+                        int rank, int world, uint32_t epoch, int num_ctas, c3cu_stream_t stream);
 
 #ifdef __cplusplus
 }

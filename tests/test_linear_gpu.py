@@ -93,6 +93,11 @@ def test_backward_parity(cuda_device, M, N, K, w_layout):
     assert_bf16_close(got, dW_ref, f"dW[{M},{N},{K}]")
     # fp32 output of exact bf16 products: only the summation order differs
     assert rel_err(got, dW_ref) < 1e-4
+    # bf16 dW (the data-parallel gradient format): fp32 accumulation, one rounding
+    dWb = linear.grad_weight(dZ, X, w_layout, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    gotb = f32(dWb) if w_layout == "nk" else f32(dWb).T
+    assert_bf16_close(gotb, dW_ref, f"dW bf16[{M},{N},{K}]")
 
 
 def test_forward_mask_from_forward_feeds_backward(cuda_device):

@@ -44,10 +44,30 @@ def _worker(rank, world, port, q):
             ar.allreduce_(3000, n + 7)
             torch.cuda.synchronize()
             results[trial] = float((ar.data() - ref).abs().max() / ref.abs().max())
+        # bf16 region (fp32 accumulation in the switch, one rounding) and fp32 region in one call
+        nb, nf = 1 << 20, 1024
+        arb = NvlsAllReduce(nf, dev, num_ctas=8, numel_bf16=nb)
+        for trial in range(2):
+            g = torch.Generator(device=dev).manual_seed(7 + 10 * trial + rank)
+            xb = torch.randn(nb, generator=g, device=dev).to(torch.bfloat16)
+            xf = torch.randn(nf, generator=g, device=dev)
+            arb.bf16.copy_(xb)
+            arb.f32.copy_(xf)
+            ref_b = xb.float()
+            ref_f = xf.clone()
+            dist.all_reduce(ref_b)
+            dist.all_reduce(ref_f)
+            arb.allreduce2_((0, nb // 2), None)
+            arb.allreduce2_((nb // 2, nb), (0, nf))
+            torch.cuda.synchronize()
+            err_b = (arb.bf16.float() - ref_b).abs()
+            ok_b = bool((err_b <= 2.0 ** -8 * ref_b.abs() + 1e-6).all())
+            results[f"bf16_{trial}"] = 0.0 if ok_b else float(err_b.max())
+            results[f"f32_{trial}"] = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max())
         c3_b200.fault_status()
         q.put((rank, "ok", results))
         dist.barrier()
-        del ar
+        del ar, arb
         dist.destroy_process_group()
     except Exception as exc:  # report to the parent instead of hanging it
         q.put((rank, "error", repr(exc)))
@@ -68,5 +88,6 @@ def test_nvls_allreduce_matches_nccl(cuda_device):
         p.join(timeout=60)
     for rank, status, res in out:
         assert status == "ok", f"rank {rank}: {res}"
-        # fp32 sums of two values: the switch and NCCL may round in a different order
+        # fp32 sums of two values: the switch and NCCL may round in a different order;
+        # bf16 results are within one bf16 rounding of the exact fp32 sum (0.0 when so)
         assert all(v <= 1e-6 for v in res.values()), res
