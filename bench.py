@@ -262,7 +262,7 @@ def run_c3(args):
     # Data-parallel overlap: the dW GEMM runs in `chunks` row bands of dW; each band's
     # all-reduce starts on the comm stream as soon as its GEMM ends (the last band carries
     # db). `reserve` SMs are left to the collective while the dX GEMM overlaps it.
-    chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "2" if world > 1 else "1")))
+    chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "1")))
     reserve = int(os.environ.get("C3_BENCH_AR_SMS", "0")) if world > 1 else 0
     if N % (chunks * 8) != 0:
         chunks = 1

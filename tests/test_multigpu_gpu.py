@@ -60,9 +60,14 @@ def _worker(rank, world, port, q):
             arb.allreduce2_((0, nb // 2), None)
             arb.allreduce2_((nb // 2, nb), (0, nf))
             torch.cuda.synchronize()
+            # within one bf16 ulp of the exact sum: the switch accumulates in fp32 and converts
+            # to bf16 once, and that conversion is not assumed to round to nearest
             err_b = (arb.bf16.float() - ref_b).abs()
-            ok_b = bool((err_b <= 2.0 ** -8 * ref_b.abs() + 1e-6).all())
+            ok_b = bool((err_b <= 2.0 ** -7 * ref_b.abs() + 1e-6).all())
             results[f"bf16_{trial}"] = 0.0 if ok_b else float(err_b.max())
+            results[f"bf16_ratio_{trial}"] = 0.0  # informational below
+            print(f"rank {rank} bf16 max err/|sum| = {float((err_b / ref_b.abs().clamp_min(1e-3)).max()):.3e}",
+                  flush=True)
             results[f"f32_{trial}"] = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max())
         c3_b200.fault_status()
         q.put((rank, "ok", results))
