@@ -206,11 +206,12 @@ def run_c3(args):
                                 device_id=dev)
 
     import c3_b200
-    from c3_b200 import _lib, linear
-    L = c3_b200.load()
+    from c3_b200.data_parallel import LinearReluTrainStep, env_grad_dtype, shard_rows
+    c3_b200.load()
     c3_b200.device_check()
 
-    M = M_GLOBAL // world
+    r_lo, r_hi = shard_rows(M_GLOBAL, world, rank)
+    M = r_hi - r_lo
     N, K = N_DIM, K_DIM
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     X = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
@@ -218,109 +219,37 @@ def run_c3(args):
          * 0.02).to(torch.bfloat16)
     b = torch.randn((N,), generator=torch.Generator(device=dev).manual_seed(98), device=dev) * 0.01
     dY = (torch.randn((M, N), generator=g, device=dev) * 1e-3).to(torch.bfloat16)
-    Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
-    dZ = torch.empty_like(dY)
     # Gradients: dW in bf16 (fp32 accumulation in the GEMM, one rounding) and db in fp32 by
     # default; C3_GRAD_DTYPE=fp32 keeps dW in fp32. With N > 1 both live in NVLink-multicast
     # (symmetric) memory and are summed in the switch by the library's all-reduce kernel
-    # (fp32 accumulation for bf16), unless C3_ALLREDUCE=nccl.
-    grad_bf16 = os.environ.get("C3_GRAD_DTYPE", "bf16") == "bf16"
-    collective = os.environ.get("C3_ALLREDUCE", "nvls") if world > 1 else "none"
-    nvls = None
-    if collective == "nvls":
-        try:
-            from c3_b200.collective import NvlsAllReduce
-            ctas = int(os.environ.get("C3_NVLS_CTAS", "16"))
-            if grad_bf16:
-                nvls = NvlsAllReduce(N, dev, num_ctas=ctas, numel_bf16=N * K)
-                dW, db = nvls.bf16.view(N, K), nvls.f32
-            else:
-                nvls = NvlsAllReduce(N * K + N, dev, num_ctas=ctas)
-                grads = nvls.data()
-                dW, db = grads[: N * K].view(N, K), grads[N * K:]
-        except Exception as exc:  # no multicast support: NCCL all-reduce instead
-            print(f"warning: NVLS all-reduce unavailable ({exc}); using NCCL", file=sys.stderr)
-            collective = "nccl"
-            nvls = None
-    if nvls is None:
-        if grad_bf16:
-            dW = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
-            db = torch.empty(N, dtype=torch.float32, device=dev)
-        else:
-            grads = torch.empty(N * K + N, dtype=torch.float32, device=dev)
-            dW, db = grads[: N * K].view(N, K), grads[N * K:]
-    dW_epi = _lib.EPI_STORE_BF16 if grad_bf16 else _lib.EPI_STORE_F32
-    dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
-
-    comp = torch.cuda.current_stream(dev)
-    comm = torch.cuda.Stream(dev)
-    ev_ar_done = torch.cuda.Event()
-    kinds = ("fwd", "prepass", "dw", "dx")
-    kernel_events = {k: [] for k in kinds}
-    ar_events = []
+    # (fp32 accumulation for bf16), unless C3_ALLREDUCE=nccl (process-group all_reduce).
+    grad_dtype = env_grad_dtype()
+    grad_bf16 = grad_dtype == torch.bfloat16
+    ar_env = os.environ.get("C3_ALLREDUCE", "nvls")
+    if ar_env not in ("nvls", "nccl", "group"):
+        raise ValueError(f"C3_ALLREDUCE must be nvls, nccl or group, got {ar_env!r}")
     # Data-parallel overlap: the dW GEMM runs in `chunks` row bands of dW; each band's
     # all-reduce starts on the comm stream as soon as its GEMM ends (the last band carries
     # db). `reserve` SMs are left to the collective while the dX GEMM overlaps it.
     chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "1")))
     reserve = int(os.environ.get("C3_BENCH_AR_SMS", "0")) if world > 1 else 0
-    if N % (chunks * 8) != 0:
-        chunks = 1
-    band = N // chunks
-    ev_band = [torch.cuda.Event() for _ in range(chunks)]
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
+                                collective="auto" if ar_env == "nvls" else ar_env,
+                                chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", "16")),
+                                reserve_sms=reserve)
+    chunks = len(train.bands)
+    collective = "none" if world == 1 else train.sync.collective
+    comp = torch.cuda.current_stream(dev)
+    kinds = train.PHASES
+    kernel_events = {k: [] for k in kinds}
+    ar_events = []
 
     def step(record: bool):
-        evs = {}
-        def mark(name):
-            if record:
-                e = torch.cuda.Event(enable_timing=True)
-                e.record(comp)
-                evs.setdefault(name, []).append(e)
-        mark("fwd"); linear.forward(X, W, b, "nk", Y, mask); mark("fwd")
-        mark("prepass"); linear.relu_mask_db(dY, mask, dZ, db); mark("prepass")
-        mark("dw")
-        ar = []
-        for c in range(chunks):
-            r0, r1 = c * band, (c + 1) * band
-            linear.gemm(dZ[:, r0:r1], X, True, True, dW_epi, dW[r0:r1], M=r1 - r0, N=K, K=M)
-            if world > 1:
-                ev_band[c].record(comp)
-                with torch.cuda.stream(comm):
-                    comm.wait_event(ev_band[c])
-                    e0 = torch.cuda.Event(enable_timing=True) if record else None
-                    if record:
-                        e0.record(comm)
-                    last = c == chunks - 1
-                    if nvls is not None and grad_bf16:
-                        nvls.allreduce2_((r0 * K, r1 * K), (0, N) if last else None, comm)
-                    elif nvls is not None:
-                        nvls.allreduce_(r0 * K, r1 * K if not last else N * K + N, comm)
-                    elif grad_bf16:
-                        dist.all_reduce(dW[r0:r1])
-                        if last:
-                            dist.all_reduce(db)
-                    else:
-                        dist.all_reduce(grads[r0 * K:(r1 * K if not last else N * K + N)])
-                    if record:
-                        e1 = torch.cuda.Event(enable_timing=True)
-                        e1.record(comm)
-                        ar.append((e0, e1))
-        mark("dw")
-        if world > 1:
-            with torch.cuda.stream(comm):
-                ev_ar_done.record(comm)
-        if reserve:
-            L.c3cu_set_gemm_max_ctas(sms - reserve)
-        mark("dx"); linear.grad_input(dZ, W, "nk", dX); mark("dx")
-        if reserve:
-            L.c3cu_set_gemm_max_ctas(0)
-        if world > 1:
-            comp.wait_event(ev_ar_done)
+        evs = train(X, W, b, dY, record=record)
         if record:
             for k in kinds:
-                kernel_events[k].append((evs[k][0], evs[k][1]))
-            ar_events.append(ar)
+                kernel_events[k].append(evs.phases[k])
+            ar_events.append(evs.allreduce)
 
     for _ in range(max(args.warmup, 0)):
         step(False)
@@ -370,7 +299,7 @@ def run_c3(args):
     # ------------------------------------------------------------------ e2e (host buffers)
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L)
+        e2e = run_e2e(args, dev, world, rank, comp, X, W, b, dY)
 
     if rank == 0:
         line = {
@@ -387,7 +316,9 @@ def run_c3(args):
                        "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
                        "allreduce": {"nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce, "
                                              "multimem.ld_reduce/st) on torch symmetric memory",
-                                     "nccl": "NCCL all_reduce", "none": "none"}[collective]},
+                                     "nccl": "NCCL through c3cu_allreduce_grads",
+                                     "group": "torch.distributed all_reduce (NCCL)",
+                                     "none": "none"}[collective]},
             "frac_of_peak": value / world / peak,
             "kernel_ms": ktime,
             "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",
@@ -398,7 +329,7 @@ def run_c3(args):
                          "frac_of_sustained": achieved / peak_sust,
                          "frac_of_spec_2250": achieved / 2250.0,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None},
-            "gpu_launches": (4 + (chunks - 1) + (chunks if nvls is not None else 0)) * args.steps,
+            "gpu_launches": (4 + (chunks - 1) + (chunks if collective == "nvls" else 0)) * args.steps,
             "clocks": sampler.record(),
         }
         if e2e is not None:
@@ -406,13 +337,14 @@ def run_c3(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
+    train.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
 
 
-def run_e2e(args, dev, world, rank, comp, comm, X, W, b, dY, L):
+def run_e2e(args, dev, world, rank, comp, X, W, b, dY):
     """The same step through the C ABI with host (pinned) buffers: every step copies the
     step's inputs host->device and the results device->host inside the timed region."""
     import torch

@@ -18,6 +18,7 @@ ERR_NAMES = {-1: "INVALID", -2: "ALIGN", -3: "CUDA", -4: "FAULT", -5: "UNSUPPORT
              -6: "WORKSPACE"}
 
 W_NK, W_KN = 0, 1
+DTYPE_F32, DTYPE_BF16 = 0, 1
 EPI_BIAS_RELU_MASK, EPI_STORE_BF16, EPI_STORE_F32, EPI_BIAS_STORE_F32 = 0, 1, 2, 3
 
 
@@ -54,6 +55,11 @@ _SIGNATURES = {
     "c3cu_convert": ([_vp, _i, _vp, _i, _i64, _vp], _i),
     "c3cu_set_gemm_max_ctas": ([_i], _i),
     "c3cu_nvls_allreduce": ([_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, ctypes.c_uint32, _i, _vp], _i),
+    "c3cu_nccl_version": ([ctypes.POINTER(_i)], _i),
+    "c3cu_nccl_unique_id": ([_vp], _i),
+    "c3cu_nccl_comm_init": ([ctypes.POINTER(_vp), _vp, _i, _i], _i),
+    "c3cu_nccl_comm_destroy": ([_vp], _i),
+    "c3cu_allreduce_grads": ([_vp, _i64, _i, _vp, _vp], _i),
     "c3cu_nvls_allreduce_f32": ([_vp, _vp, _vp, _i64, _i64, _i, _i, ctypes.c_uint32, _i, _vp], _i),
     "c3cu_relu_mask_db_noalloc": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp], _i),
     "c3cu_flash_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _i, _vp], _i),

@@ -27,7 +27,7 @@ CXX_FLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-Wextra", f"-I{ROOT / 'incl
 
 def _sources():
     cu = sorted(CSRC.glob("*.cu"))
-    cpp = sorted(HOST.rglob("*.cpp")) if HOST.exists() else []
+    cpp = sorted(CSRC.glob("*.cpp")) + (sorted(HOST.rglob("*.cpp")) if HOST.exists() else [])
     return cu, cpp
 
 

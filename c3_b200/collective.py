@@ -93,3 +93,46 @@ class NvlsAllReduce:
                                              ctypes.c_void_p(s.cuda_stream))
         _lib.check(rc, "c3cu_nvls_allreduce")
         self.epoch += 1
+
+
+class NcclComm:
+    """An NCCL communicator made through the library's C ABI (c3cu_nccl_comm_init) and the
+    gradient all-reduce on it (c3cu_allreduce_grads) — the same calls a C++ host of the C3
+    API makes. Rank 0's unique id travels to the other ranks over the process group."""
+
+    def __init__(self, device: torch.device, group=None):
+        self.group = group or dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.device = torch.device(device)
+        L = _lib.load()
+        uid = torch.zeros(128, dtype=torch.uint8)
+        if self.rank == 0:
+            raw = ctypes.create_string_buffer(128)
+            _lib.check(L.c3cu_nccl_unique_id(raw), "c3cu_nccl_unique_id")
+            uid.copy_(torch.frombuffer(bytearray(raw.raw), dtype=torch.uint8))
+        backend = dist.get_backend(self.group)
+        t = uid.to(self.device) if backend == "nccl" else uid
+        dist.broadcast(t, group_src=0, group=self.group)
+        raw = bytes(t.cpu().numpy().tobytes())
+        comm = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(L.c3cu_nccl_comm_init(ctypes.byref(comm), raw, self.world, self.rank),
+                       "c3cu_nccl_comm_init")
+        self.comm = comm
+
+    def allreduce_(self, t: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """In-place sum of a contiguous fp32 or bf16 CUDA tensor over the communicator."""
+        if not t.is_cuda or not t.is_contiguous() or t.dtype not in (torch.float32, torch.bfloat16):
+            raise _lib.C3CUError(-1, "allreduce_grads", "expected a contiguous fp32/bf16 CUDA tensor")
+        s = stream or torch.cuda.current_stream(t.device)
+        dt = _lib.DTYPE_F32 if t.dtype == torch.float32 else _lib.DTYPE_BF16
+        rc = _lib.load().c3cu_allreduce_grads(ctypes.c_void_p(t.data_ptr()), t.numel(), dt, self.comm,
+                                              ctypes.c_void_p(s.cuda_stream))
+        _lib.check(rc, "c3cu_allreduce_grads")
+        return t
+
+    def close(self):
+        if self.comm:
+            _lib.check(_lib.load().c3cu_nccl_comm_destroy(self.comm), "c3cu_nccl_comm_destroy")
+            self.comm = None

@@ -1,0 +1,260 @@
+"""Data-parallel composition of the captured Linear+bias+ReLU training step.
+
+The reference runs one process on one CPU; its captured backward of the MatMul+Add+ReLU region
+(src/C3/C3BackwardCapture.cpp:501-528 ReLU backward, :618-644 Add backward, :681-723 MatMul
+backward) is what each rank runs here on its own rows:
+
+    dZ  = mask * dY,  db_r = sum_rows(dZ)          (pre-pass, one kernel)
+    dW_r = dZᵀ X                                   (tcgen05 GEMM; bf16 or fp32 out)
+    dX  = dZ W                                     (tcgen05 GEMM; needs no exchange)
+
+and the one exchange step of the path is the sum of [dW ‖ db] over the ranks. Rows of X / dY /
+mask are split contiguously (`shard_rows`); W and b are replicated. The dW GEMM may run in row
+bands of dW (`dw_bands`): each band's all-reduce starts on a communication stream as soon as
+its GEMM ends, overlapped with the remaining bands and with the dX GEMM.
+
+`GradientSync` owns one rank's dW / db and sums them:
+- "nvls": the library's in-switch all-reduce on NVLink-multicast memory (c3_b200.collective);
+- "nccl": NCCL through the library's C ABI (c3cu_allreduce_grads on a communicator made by
+  c3cu_nccl_comm_init), as a C++ host calls it;
+- "group": torch.distributed all_reduce on the process group (NCCL for CUDA tensors, gloo for
+  host tensors — the host-side path the CPU tests exercise).
+"""
+from __future__ import annotations
+
+import os
+import sys
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(m_global: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous rows [lo, hi) of rank `rank`; the first m_global % world ranks get one more."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if m_global < 0:
+        raise ValueError("negative row count")
+    base, extra = divmod(m_global, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def dw_bands(n: int, chunks: int, align: int = 8) -> list[tuple[int, int]]:
+    """Row bands of dW [n, K] for the banded dW GEMM + all-reduce schedule.
+
+    Each band holds a multiple of `align` rows (the bf16 in-switch all-reduce moves 8 elements
+    per access and the GEMM's output tile is 8-row aligned); when n does not split into
+    `chunks` such bands, one band covers all of dW."""
+    if chunks <= 1 or n % (chunks * align) != 0:
+        return [(0, n)]
+    band = n // chunks
+    return [(c * band, (c + 1) * band) for c in range(chunks)]
+
+
+class GradientSync:
+    """dW [N, K] (bf16 or fp32) and db [N] (fp32) of one rank, summed over a process group."""
+
+    def __init__(self, n: int, k: int, device: torch.device, grad_dtype: torch.dtype = torch.bfloat16,
+                 collective: str = "auto", group=None, num_ctas: int = 16):
+        if grad_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError(f"dW dtype must be bfloat16 or float32, got {grad_dtype}")
+        if collective not in ("auto", "nvls", "nccl", "group"):
+            raise ValueError(f"collective must be 'auto', 'nvls', 'nccl' or 'group', got {collective!r}")
+        self.n, self.k = n, k
+        self.device = torch.device(device)
+        self.grad_dtype = grad_dtype
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.nvls = None
+        self.nccl = None
+        want_nvls = collective == "nvls" or (collective == "auto" and self.device.type == "cuda"
+                                             and self.world > 1)
+        if want_nvls:
+            try:
+                from .collective import NvlsAllReduce
+                if grad_dtype == torch.bfloat16:
+                    self.nvls = NvlsAllReduce(n, self.device, group=group, num_ctas=num_ctas,
+                                              numel_bf16=n * k)
+                    self.dW, self.db = self.nvls.bf16.view(n, k), self.nvls.f32
+                else:
+                    self.nvls = NvlsAllReduce(n * k + n, self.device, group=group, num_ctas=num_ctas)
+                    flat = self.nvls.data()
+                    self.dW, self.db = flat[: n * k].view(n, k), flat[n * k:]
+            except Exception as exc:
+                if collective == "nvls":
+                    raise
+                print(f"warning: NVLS all-reduce unavailable ({exc}); using the process group",
+                      file=sys.stderr)
+                self.nvls = None
+        if collective == "nccl" and self.world > 1:
+            from .collective import NcclComm
+            self.nccl = NcclComm(self.device, group)
+        self.collective = "nvls" if self.nvls is not None else ("nccl" if self.nccl else "group")
+        if self.nvls is None:
+            if grad_dtype == torch.bfloat16:
+                self.dW = torch.empty((n, k), dtype=grad_dtype, device=self.device)
+                self.db = torch.empty(n, dtype=torch.float32, device=self.device)
+            else:
+                flat = torch.empty(n * k + n, dtype=torch.float32, device=self.device)
+                self.dW, self.db = flat[: n * k].view(n, k), flat[n * k:]
+        self._flat_f32 = None if grad_dtype == torch.bfloat16 else flat
+
+    def reduce_(self, rows: tuple[int, int] | None = None, with_db: bool = True, stream=None):
+        """Sum dW rows [lo, hi) (all rows by default) and, with `with_db`, db over the group.
+
+        Enqueued on `stream` (CUDA tensors; default: the current stream). With one rank this is
+        a no-op."""
+        if self.world == 1:
+            return
+        lo, hi = rows if rows is not None else (0, self.n)
+        if not 0 <= lo <= hi <= self.n:
+            raise ValueError(f"dW rows [{lo}, {hi}) outside [0, {self.n})")
+        k, n = self.k, self.n
+        if self.nvls is not None:
+            if self.grad_dtype == torch.bfloat16:
+                self.nvls.allreduce2_((lo * k, hi * k) if hi > lo else None,
+                                      (0, n) if with_db else None, stream)
+            elif with_db and hi == n:
+                self.nvls.allreduce_(lo * k, n * k + n, stream)
+            else:
+                if hi > lo:
+                    self.nvls.allreduce_(lo * k, hi * k, stream)
+                if with_db:
+                    self.nvls.allreduce_(n * k, n * k + n, stream)
+            return
+        if self.nccl is not None:
+            if self._flat_f32 is not None and with_db and hi == n:
+                self.nccl.allreduce_(self._flat_f32[lo * k:], stream)
+                return
+            if hi > lo:
+                self.nccl.allreduce_(self.dW[lo:hi], stream)
+            if with_db:
+                self.nccl.allreduce_(self.db, stream)
+            return
+        ctx = torch.cuda.stream(stream) if (stream is not None and self.device.type == "cuda") else _Null()
+        with ctx:
+            if self._flat_f32 is not None and with_db and hi == n:
+                dist.all_reduce(self._flat_f32[lo * k:], group=self.group)
+                return
+            if hi > lo:
+                dist.all_reduce(self.dW[lo:hi], group=self.group)
+            if with_db:
+                dist.all_reduce(self.db, group=self.group)
+
+    def close(self):
+        """Releases the NCCL communicator (before the process group is destroyed)."""
+        if self.nccl is not None:
+            self.nccl.close()
+            self.nccl = None
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+@dataclass
+class StepEvents:
+    """CUDA events of one recorded step: (start, end) per phase on the compute stream and
+    (start, end) per all-reduce band on the communication stream."""
+    phases: dict
+    allreduce: list
+
+
+class LinearReluTrainStep:
+    """The data-parallel captured step of Y = relu(X Wᵀ + b) on one rank's rows.
+
+    forward (Y bf16 + bit-packed ReLU mask) → pre-pass (dZ, db) → dW GEMM in bands, each band's
+    all-reduce on `comm` → dX GEMM → the compute stream waits for the last all-reduce.
+    `reserve_sms` SMs are left to the collective while the dX GEMM overlaps it."""
+
+    PHASES = ("fwd", "prepass", "dw", "dx")
+
+    def __init__(self, m: int, n: int, k: int, device: torch.device, grad_dtype=torch.bfloat16,
+                 collective: str = "auto", group=None, chunks: int = 1, num_ctas: int = 16,
+                 reserve_sms: int = 0):
+        from . import _lib
+        self.m, self.n, self.k = m, n, k
+        self.device = torch.device(device)
+        self.sync = GradientSync(n, k, self.device, grad_dtype, collective, group, num_ctas)
+        self.world = self.sync.world
+        self.bands = dw_bands(n, chunks)
+        self.reserve_sms = reserve_sms if self.world > 1 else 0
+        self.epi = _lib.EPI_STORE_BF16 if grad_dtype == torch.bfloat16 else _lib.EPI_STORE_F32
+        dev = self.device
+        self.Y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        self.mask = torch.empty((m, (n + 31) // 32), dtype=torch.int32, device=dev)
+        self.dZ = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        self.dX = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+        self.comm = torch.cuda.Stream(dev)
+        self._ev_band = [torch.cuda.Event() for _ in self.bands]
+        self._ev_done = torch.cuda.Event()
+        self._sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def close(self):
+        self.sync.close()
+
+    @property
+    def dW(self) -> torch.Tensor:
+        return self.sync.dW
+
+    @property
+    def db(self) -> torch.Tensor:
+        return self.sync.db
+
+    def __call__(self, X, W, b, dY, record: bool = False) -> StepEvents | None:
+        from . import _lib, linear
+        comp = torch.cuda.current_stream(self.device)
+        phases: dict = {}
+        ar: list = []
+
+        def mark(name):
+            if record:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(comp)
+                phases.setdefault(name, []).append(e)
+
+        mark("fwd"); linear.forward(X, W, b, "nk", self.Y, self.mask); mark("fwd")
+        mark("prepass"); linear.relu_mask_db(dY, self.mask, self.dZ, self.db); mark("prepass")
+        mark("dw")
+        m, k = self.m, self.k
+        for i, (r0, r1) in enumerate(self.bands):
+            linear.gemm(self.dZ[:, r0:r1], X, True, True, self.epi, self.dW[r0:r1], M=r1 - r0, N=k, K=m)
+            if self.world > 1:
+                self._ev_band[i].record(comp)
+                self.comm.wait_event(self._ev_band[i])
+                if record:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(self.comm)
+                self.sync.reduce_((r0, r1), with_db=i == len(self.bands) - 1, stream=self.comm)
+                if record:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(self.comm)
+                    ar.append((e0, e1))
+        mark("dw")
+        if self.world > 1:
+            self._ev_done.record(self.comm)
+        lib = _lib.load() if self.reserve_sms else None
+        if lib is not None:
+            lib.c3cu_set_gemm_max_ctas(self._sms - self.reserve_sms)
+        mark("dx"); linear.grad_input(self.dZ, W, "nk", self.dX); mark("dx")
+        if lib is not None:
+            lib.c3cu_set_gemm_max_ctas(0)
+        if self.world > 1:
+            comp.wait_event(self._ev_done)
+        if record:
+            return StepEvents({p: (phases[p][0], phases[p][1]) for p in self.PHASES}, ar)
+        return None
+
+
+def env_grad_dtype() -> torch.dtype:
+    """C3_GRAD_DTYPE=bf16 (default) | fp32."""
+    v = os.environ.get("C3_GRAD_DTYPE", "bf16")
+    if v not in ("bf16", "fp32"):
+        raise ValueError(f"C3_GRAD_DTYPE must be bf16 or fp32, got {v!r}")
+    return torch.bfloat16 if v == "bf16" else torch.float32

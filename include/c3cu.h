@@ -211,6 +211,20 @@ int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint32_t* local_
                         int64_t bf16_offset, int64_t bf16_count, int64_t f32_offset, int64_t f32_count,
                         int rank, int world, uint32_t epoch, int num_ctas, c3cu_stream_t stream);
 
+/* Gradient all-reduce (sum, in place) through an NCCL communicator: `count` elements of
+ * `dtype` (C3CU_DTYPE_F32 or C3CU_DTYPE_BF16) at `grads` on `stream`. `comm` is an
+ * ncclComm_t, e.g. from c3cu_nccl_comm_init, whose id rank 0 made with c3cu_nccl_unique_id
+ * (128 bytes) and the host passed to every rank. NCCL is loaded at run time ("libnccl.so.2",
+ * the copy already in the process if any); without it these calls return
+ * C3CU_ERR_UNSUPPORTED. This is the exchange step of the data-parallel training step, named
+ * in the hot path's C ABI (dW || db after c3cu_gemm_dw / c3cu_relu_mask_db); the reference
+ * itself has no collective. */
+int c3cu_nccl_version(int* version);
+int c3cu_nccl_unique_id(void* id_out /* 128 bytes */);
+int c3cu_nccl_comm_init(void** comm_out, const void* id, int world, int rank);
+int c3cu_nccl_comm_destroy(void* comm);
+int c3cu_allreduce_grads(void* grads, int64_t count, int dtype, void* comm, c3cu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,161 @@
+"""Host logic of the data-parallel step on CPU: row sharding, dW band schedule, and the
+gradient sum over a world_size-2 gloo process group (c3_b200.data_parallel.GradientSync,
+"group" collective), checked against the oracle's full-batch backward of the MatMul+Add+ReLU
+region (src/C3/C3BackwardCapture.cpp:501-528, 618-644, 681-723). Each rank's local gradients
+come from the oracle on its rows; the test checks that the sharding and the banded sums
+reassemble the full-batch gradients. A rank that leaves before the exchange makes the other
+rank's sum end with an error instead of hanging it."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from c3_b200.data_parallel import dw_bands, shard_rows
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("m,world", [(0, 1), (1, 2), (7, 2), (16384, 8), (37, 4), (5, 8), (129, 3)])
+def test_shard_rows_cover_and_balance(m, world):
+    ranges = [shard_rows(m, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == m
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0, "ranges must be contiguous"
+    sizes = [hi - lo for lo, hi in ranges]
+    assert max(sizes) - min(sizes) <= 1
+    assert sizes == sorted(sizes, reverse=True)
+
+
+def test_shard_rows_rejects_bad_rank():
+    with pytest.raises(ValueError):
+        shard_rows(10, 2, 2)
+    with pytest.raises(ValueError):
+        shard_rows(10, 0, 0)
+
+
+@pytest.mark.parametrize("n,chunks,expect", [
+    (4096, 1, [(0, 4096)]),
+    (4096, 4, [(0, 1024), (1024, 2048), (2048, 3072), (3072, 4096)]),
+    (24, 3, [(0, 8), (8, 16), (16, 24)]),
+    (20, 2, [(0, 20)]),      # 10-row bands are not 8-row aligned: one band
+    (4096, 0, [(0, 4096)]),
+])
+def test_dw_bands(n, chunks, expect):
+    assert dw_bands(n, chunks) == expect
+
+
+def _problem(M, N, K, seed=5):
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    Z = rng.standard_normal((M, N)).astype(np.float32)  # pre-activation of the forward
+    Z[::5, ::3] = 0.0                                    # ReLU'(0) = 0 (CmpF OGT)
+    dY = (rng.standard_normal((M, N)) * 1e-2).astype(np.float32)
+    return X, Z, dY
+
+
+def _local_grads(X, Z, dY, lo, hi):
+    import oracle
+    dZ = oracle.relu_bwd(dY[lo:hi], Z[lo:hi])
+    dW = oracle.matmul(dZ, X[lo:hi], transA=True) if hi > lo else np.zeros((dY.shape[1], X.shape[1]), np.float32)
+    db = oracle.sum_reduce(dZ, 0) if hi > lo else np.zeros(dY.shape[1], np.float32)
+    return dW, db
+
+
+def _worker(rank, world, port, q, mode):
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        from c3_b200.data_parallel import GradientSync
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=20))
+        M, N, K = 37, 24, 20
+        X, Z, dY = _problem(M, N, K)
+        lo, hi = shard_rows(M, world, rank)
+        dW_r, db_r = _local_grads(X, Z, dY, lo, hi)
+        if mode == "leave":
+            # rank 1 leaves between steps, before its exchange; rank 0's sum must end with an
+            # error (peer closed or process-group timeout), not wait for ever
+            if rank == 1:
+                q.put((rank, "ok", "left"))
+                return
+            sync = GradientSync(N, K, torch.device("cpu"), torch.float32, "group")
+            sync.dW.copy_(torch.from_numpy(dW_r))
+            sync.db.copy_(torch.from_numpy(db_r))
+            try:
+                sync.reduce_()
+            except Exception as exc:  # the failure surfaced on the host
+                q.put((rank, "ok", f"detected: {type(exc).__name__}"))
+                return
+            q.put((rank, "error", "the sum returned although the peer left"))
+            return
+        out = {}
+        for chunks in (1, 3):
+            sync = GradientSync(N, K, torch.device("cpu"), torch.float32, "group")
+            sync.dW.copy_(torch.from_numpy(dW_r))
+            sync.db.copy_(torch.from_numpy(db_r))
+            bands = dw_bands(N, chunks)
+            for i, band in enumerate(bands):
+                sync.reduce_(band, with_db=i == len(bands) - 1)
+            out[chunks] = (sync.dW.numpy().copy(), sync.db.numpy().copy())
+        q.put((rank, "ok", out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc)))
+
+
+def _run(world, mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        out = [q.get(timeout=120) for _ in procs]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return {rank: (status, res) for rank, status, res in out}
+
+
+def test_gradient_sum_world2_gloo():
+    import oracle
+    res = _run(2, "sum")
+    M, N, K = 37, 24, 20
+    X, Z, dY = _problem(M, N, K)
+    dW_full, db_full = _local_grads(X, Z, dY, 0, M)
+    # sequential-k fp32 sums over all rows vs the sum of two partial sums: bounded by a few
+    # ulp of the sum of |terms|
+    dZ = oracle.relu_bwd(dY, Z)
+    bound_w = 1e-6 * (np.abs(dZ).T @ np.abs(X)) + 1e-12
+    bound_b = 1e-6 * np.abs(dZ).sum(axis=0) + 1e-12
+    for rank in range(2):
+        status, out = res[rank]
+        assert status == "ok", f"rank {rank}: {out}"
+        for chunks, (dW, db) in out.items():
+            assert (np.abs(dW - dW_full) <= bound_w).all(), f"rank {rank}, {chunks} band(s): dW"
+            assert (np.abs(db - db_full) <= bound_b).all(), f"rank {rank}, {chunks} band(s): db"
+        # both ranks hold the same bits after the sum
+    for chunks in res[0][1]:
+        assert np.array_equal(res[0][1][chunks][0], res[1][1][chunks][0])
+
+
+def test_rank_leaving_is_detected_world2_gloo():
+    res = _run(2, "leave")
+    assert res[1] == ("ok", "left")
+    status, msg = res[0]
+    assert status == "ok", msg
+    assert msg.startswith("detected")

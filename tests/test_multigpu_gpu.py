@@ -69,6 +69,18 @@ def _worker(rank, world, port, q):
             print(f"rank {rank} bf16 max err/|sum| = {float((err_b / ref_b.abs().clamp_min(1e-3)).max()):.3e}",
                   flush=True)
             results[f"f32_{trial}"] = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max())
+        # NCCL through the C ABI (c3cu_allreduce_grads) against torch's all_reduce
+        from c3_b200.collective import NcclComm
+        nc = NcclComm(dev)
+        for dt in (torch.float32, torch.bfloat16):
+            g = torch.Generator(device=dev).manual_seed(31 + rank)
+            x = torch.randn(4099, generator=g, device=dev).to(dt)
+            ref = x.clone()
+            dist.all_reduce(ref)
+            nc.allreduce_(x)
+            torch.cuda.synchronize()
+            results[f"nccl_abi_{dt}"] = float((x.float() - ref.float()).abs().max())
+        nc.close()
         c3_b200.fault_status()
         q.put((rank, "ok", results))
         dist.barrier()
@@ -96,3 +108,82 @@ def test_nvls_allreduce_matches_nccl(cuda_device):
         # fp32 sums of two values: the switch and NCCL may round in a different order;
         # bf16 results are within one bf16 rounding of the exact fp32 sum (0.0 when so)
         assert all(v <= 1e-6 for v in res.values()), res
+
+
+def _step_worker(rank, world, port, q):
+    """The row-sharded training step (c3_b200.data_parallel.LinearReluTrainStep) on `world`
+    GPUs against the one-GPU kernels on the full batch."""
+    try:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        import c3_b200
+        from c3_b200 import linear
+        from c3_b200.data_parallel import LinearReluTrainStep, shard_rows
+        M, N, K = 1000, 512, 384
+        g = torch.Generator(device=dev).manual_seed(11)  # the same full batch on every rank
+        X = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        W = (torch.randn((N, K), generator=g, device=dev) * 0.05).to(torch.bfloat16)
+        b = torch.randn((N,), generator=g, device=dev) * 0.05
+        dY = (torch.randn((M, N), generator=g, device=dev) * 1e-2).to(torch.bfloat16)
+        lo, hi = shard_rows(M, world, rank)
+        res = {}
+        for grad_dtype, chunks, coll in ((torch.bfloat16, 1, "nvls"), (torch.bfloat16, 4, "nvls"),
+                                         (torch.float32, 2, "nvls"), (torch.bfloat16, 2, "nccl"),
+                                         (torch.float32, 1, "nccl")):
+            step = LinearReluTrainStep(hi - lo, N, K, dev, grad_dtype, collective=coll, chunks=chunks,
+                                       num_ctas=8)
+            Xs, dYs = X[lo:hi].contiguous(), dY[lo:hi].contiguous()
+            step(Xs, W, b, dYs)
+            step(Xs, W, b, dYs)  # a second step re-uses the buffers and the barrier epochs
+            torch.cuda.synchronize()
+            # one-GPU reference on the full batch (fp32 dW), and this rank's fp32 partial
+            Y, mask = linear.forward(X, W, b, "nk")
+            dZ, db = linear.relu_mask_db(dY, mask)
+            dW = linear.grad_weight(dZ, X, "nk")
+            dX = linear.grad_input(dZ, W, "nk")
+            part = linear.grad_weight(dZ[lo:hi].contiguous(), Xs, "nk").abs()
+            dist.all_reduce(part)  # sum over ranks of |partial dW|
+            torch.cuda.synchronize()
+            tol = (2.0 ** -6 if grad_dtype == torch.bfloat16 else 1e-5) * part + 1e-6
+            key = f"{grad_dtype}_{chunks}_{coll}"
+            res[key + "_collective"] = step.sync.collective == coll
+            res[key + "_dW_ok"] = bool(((step.dW.float() - dW).abs() <= tol).all())
+            res[key + "_db_err"] = float((step.db - db).abs().max() / db.abs().max())
+            res[key + "_dX_equal"] = bool(torch.equal(step.dX, dX[lo:hi]))
+            res[key + "_Y_equal"] = bool(torch.equal(step.Y, Y[lo:hi]))
+            step.close()
+            del step
+        c3_b200.fault_status()
+        q.put((rank, "ok", res))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc)))
+
+
+def test_sharded_step_matches_full_batch(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_step_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, res in out:
+        assert status == "ok", f"rank {rank}: {res}"
+        for key, v in res.items():
+            if key.endswith("_collective") or key.endswith("_ok") or key.endswith("_equal"):
+                assert v is True, (key, res)
+            else:  # db: fp32 sums of two row blocks vs one pass, and summation order
+                assert v <= 1e-5, (key, res)
