@@ -2,6 +2,7 @@
 // Linear+bias+ReLU forward, the dX / dW backward GEMMs and the general bf16 GEMM.
 #include <atomic>
 
+#include "gemm2_tcgen05.cuh"
 #include "gemm_tcgen05.cuh"
 #include "host_util.h"
 
@@ -15,6 +16,73 @@ using gemm::Params;
 // Upper bound on the persistent GEMM's CTAs (0 = one per SM). Lowering it leaves SMs free
 // for a collective that runs concurrently (e.g. an all-reduce overlapped with the dX GEMM).
 std::atomic<int> g_max_ctas{0};
+
+// Kernel variant: 0 = automatic (the CTA-pair kernel whenever M spans at least two 128-row
+// halves), 1 = single-CTA kernel only, 2 = CTA-pair kernel whenever it applies.
+std::atomic<int> g_variant{0};
+
+// Co-resident clusters of two CTAs for a kernel (cached per device and kernel).
+template <class Kern>
+int max_pair_clusters(Kern kern, uint32_t smem_bytes, int threads) {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] > 0) return cached[dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cached[dev] = n;
+  return n;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
+                cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  int rc;
+  // Per CTA: A 128 (M) x 64 (K), B 128 (N) x 64 (K); MN-major operands in 64 x 64 boxes.
+  if (!A_MN)
+    rc = encode_bf16_2d_sw128(&ta, A, p.M, p.K, lda, 64, gemm2::HM);
+  else
+    rc = encode_bf16_2d_sw128(&ta, A, p.K, p.M, lda, 64, gemm2::BK);
+  if (rc != C3CU_OK) return rc;
+  if (!B_MN)
+    rc = encode_bf16_2d_sw128(&tb, B, p.N, p.K, ldb, 64, gemm2::HN);
+  else
+    rc = encode_bf16_2d_sw128(&tb, B, p.K, p.N, ldb, 64, gemm2::BK);
+  if (rc != C3CU_OK) return rc;
+
+  auto kern = gemm2::gemm2_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          gemm2::SMEM_BYTES),
+                     "gemm2: set max dynamic shared memory");
+    if (rc != C3CU_OK) return rc;
+    attr_set = true;
+  }
+  const int tiles = ((p.M + gemm2::TM - 1) / gemm2::TM) * ((p.N + gemm2::TN - 1) / gemm2::TN);
+  int clusters = max_pair_clusters(kern, gemm2::SMEM_BYTES, gemm2::kThreads);
+  if (clusters <= 0) clusters = sm_count() / 2;
+  const int cap = g_max_ctas.load(std::memory_order_relaxed);
+  if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
+  if (tiles < clusters) clusters = tiles;
+  kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, p);
+  return cuda_status(cudaGetLastError(), "gemm2: launch");
+}
 
 template <bool A_MN, bool B_MN, int EPI>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
@@ -54,8 +122,12 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
 
 int dispatch(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
              int epi, const Params& p, cudaStream_t st) {
-#define C3CU_GEMM_CASE(AM, BMN, E) \
-  if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, st);
+  const int variant = g_variant.load(std::memory_order_relaxed);
+  const bool pair = variant != 1 && p.M > gemm2::HM;
+#define C3CU_GEMM_CASE(AM, BMN, E)                                          \
+  if (a_mn == AM && b_mn == BMN && epi == E)                                \
+    return pair ? launch_pair<AM, BMN, E>(A, lda, B, ldb, p, st)            \
+                : launch<AM, BMN, E>(A, lda, B, ldb, p, st);
   C3CU_GEMM_CASE(0, 0, kEpiBiasReluMask)
   C3CU_GEMM_CASE(0, 1, kEpiBiasReluMask)
   C3CU_GEMM_CASE(0, 0, kEpiStoreBf16)
@@ -135,6 +207,15 @@ int c3cu_set_gemm_max_ctas(int max_ctas) {
     return C3CU_ERR_INVALID;
   }
   c3cu::g_max_ctas.store(max_ctas, std::memory_order_relaxed);
+  return C3CU_OK;
+}
+
+int c3cu_set_gemm_variant(int variant) {
+  if (variant < 0 || variant > 2) {
+    c3cu::set_error("set_gemm_variant: unknown variant %d", variant);
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::g_variant.store(variant, std::memory_order_relaxed);
   return C3CU_OK;
 }
 

@@ -1,0 +1,233 @@
+// CTA-pair variant of the persistent tcgen05 GEMM (cta_group::2), same operands, majors and
+// epilogues as gemm_tcgen05.cuh:
+//
+//   D[Mg, Ng] = A[Mg, Kg] * B[Ng, Kg]^T      (fp32 accumulation in TMEM)
+//
+// A cluster of two CTAs (one TPC) computes 256 x 256 output tiles. Each CTA loads its own
+// 128 rows of A and its own 128 of the tile's 256 B rows (N), so a CTA moves 32 KiB per
+// 64-deep K block instead of 48 KiB for the single-CTA 128 x 256 tile: one third less
+// L2 -> shared-memory traffic per output element. The even CTA ("leader") issues one
+// 256 x 256 x 16 tcgen05.mma per K step, which reads both CTAs' shared memory and writes
+// each CTA's half of the accumulator rows into that CTA's TMEM.
+//
+// Roles per CTA (6 warps, one CTA per SM):
+//   warp 0      TMA producer. Both CTAs load their halves; every copy signals the leader's
+//               `full` barrier (the leader arms it with the bytes of both halves).
+//   warp 1      TMEM owner (pair allocation); in the leader also the MMA issuer. Each
+//               stage is released in both CTAs by one multicast tcgen05.commit.
+//   warps 2..5  epilogue on this CTA's 128 accumulator rows; they release an accumulator
+//               by arriving on the leader's `acc_empty` barrier (8 arrivals: both CTAs).
+// Loads use no cluster multicast: every CTA reads its own operands from global memory.
+#pragma once
+
+#include "gemm_tcgen05.cuh"
+
+namespace c3cu {
+namespace gemm2 {
+
+constexpr int TM = 256;          // output tile rows per pair (128 per CTA)
+constexpr int TN = 256;          // output tile columns per pair
+constexpr int HM = TM / 2;       // A rows per CTA
+constexpr int HN = TN / 2;       // B rows (output columns) loaded per CTA
+constexpr int BK = 64;
+constexpr int STAGES = 6;
+constexpr int UMMA_K = 16;
+constexpr int kThreads = 192;
+constexpr uint32_t A_STAGE_BYTES = HM * BK * 2;  // 16 KiB
+constexpr uint32_t B_STAGE_BYTES = HN * BK * 2;  // 16 KiB
+constexpr uint32_t STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr uint32_t MN_CHUNK_BYTES = 64 * BK * 2;
+constexpr uint32_t TMEM_COLS = 512;  // two accumulators of 128 lanes x 256 fp32 columns
+constexpr uint32_t BAR_BYTES = (2 * STAGES + 5) * 8 + 8;
+constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+constexpr uint16_t kPairMask = 0x3;
+
+template <bool A_MN, bool B_MN>
+__device__ __forceinline__ void issue_half_loads(const CUtensorMap* tma, const CUtensorMap* tmb,
+                                                 uint8_t* sa, uint8_t* sb, uint32_t bar_leader,
+                                                 int a_row0, int b_row0, int k0) {
+  if constexpr (!A_MN) {
+    tma_load_2d_pair(sa, tma, bar_leader, k0, a_row0);
+  } else {
+#pragma unroll
+    for (int j = 0; j < HM / 64; ++j)
+      tma_load_2d_pair(sa + j * MN_CHUNK_BYTES, tma, bar_leader, a_row0 + 64 * j, k0);
+  }
+  if constexpr (!B_MN) {
+    tma_load_2d_pair(sb, tmb, bar_leader, k0, b_row0);
+  } else {
+#pragma unroll
+    for (int j = 0; j < HN / 64; ++j)
+      tma_load_2d_pair(sb + j * MN_CHUNK_BYTES, tmb, bar_leader, b_row0 + 64 * j, k0);
+  }
+}
+
+// Fault path of a CTA that cannot observe the barrier its copies signal (the peer's copies
+// complete on the leader's barrier): give copies already in flight time to land before the
+// CTA's shared memory is released. A copy of a few KiB lands within microseconds.
+__device__ __forceinline__ void settle_inflight_copies() {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < 200000ull) {
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                 const gemm::Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+
+  const uint32_t warp = warp_id_sync();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const bool leader = rank == 0u;
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+
+  const int m_tiles = (p.M + TM - 1) / TM;
+  const int n_tiles = (p.N + TN - 1) / TN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tma);
+    tma_prefetch_desc(&tmb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM of the pair allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t armed = 0u, armed_par = 0u;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += num_clusters) {
+        const int m0 = (tile / n_tiles) * TM;
+        const int n0 = (tile % n_tiles) * TN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, kFaultWaitEmpty)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2u * STAGE_BYTES);
+          const uint32_t bar_leader = mapa_shared(smem_u32(&full[s]), 0u);
+          issue_half_loads<A_MN, B_MN>(&tma, &tmb, sA + s * A_STAGE_BYTES, sB + s * B_STAGE_BYTES,
+                                       bar_leader, m0 + static_cast<int>(rank) * HM,
+                                       n0 + static_cast<int>(rank) * HN, kb * BK);
+          armed |= 1u << s;
+          armed_par = (armed_par & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
+        }
+      }
+      if (!ok) {
+        if (leader) {
+          for (int t = 0; t < STAGES; ++t)
+            if (armed & (1u << t)) gemm::drain_wait(&full[t], (armed_par >> t) & 1u);
+        }
+        settle_inflight_copies();
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t IDESC = make_idesc_bf16_f32(TM, TN, A_MN, B_MN);
+      constexpr uint32_t A_KSTEP = A_MN ? UMMA_K * 128 : UMMA_K * 2;
+      constexpr uint32_t B_KSTEP = B_MN ? UMMA_K * 128 : UMMA_K * 2;
+      constexpr uint32_t A_LBO = A_MN ? MN_CHUNK_BYTES : 16;
+      constexpr uint32_t B_LBO = B_MN ? MN_CHUNK_BYTES : 16;
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t acc = 0, acc_ph = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += num_clusters) {
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, kFaultWaitAccEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * TN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, kFaultWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * B_STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t ad = make_sw128_desc(a_addr + kk * A_KSTEP, A_LBO, 1024);
+            const uint64_t bd = make_sw128_desc(b_addr + kk * B_KSTEP, B_LBO, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&empty[s], kPairMask);  // frees stage s in both CTAs
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&acc_full[acc], kPairMask);  // both halves ready for the epilogues
+        acc ^= 1u;
+        if (acc == 0u) acc_ph ^= 1u;
+      }
+      umma_commit_pair_mc(drain, 0x1);
+      gemm::drain_wait(drain, 0u);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const uint32_t q = warp & 3u;
+    uint32_t acc = 0, acc_ph = 0;
+    for (int tile = cluster; tile < num_tiles; tile += num_clusters) {
+      const int m0 = (tile / n_tiles) * TM + static_cast<int>(rank) * HM;
+      const int n0 = (tile % n_tiles) * TN;
+      if (!mbar_wait(&acc_full[acc], acc_ph, kFaultWaitAccFull)) break;
+      tc_fence_after();
+      const int row = m0 + static_cast<int>(q * 32 + lane);
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * TN;
+#pragma unroll 1
+      for (int c = 0; c < TN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= p.N) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_wait_ld();
+        gemm::epilogue_chunk<EPI>(p, r, row, col0);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0u));
+      acc ^= 1u;
+      if (acc == 0u) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // all MMAs complete (leader drained) and both epilogues done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm2
+}  // namespace c3cu

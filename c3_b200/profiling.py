@@ -1,6 +1,7 @@
 """Runs one hot-path kernel repeatedly on cuda:0, for timing and for ncu captures.
 
     python -m c3_b200.profiling <case> [--iters N] [--m M] [--n N] [--k K] [--elems E]
+                                [--variant V] [--dw-dtype bf16|fp32]
 
 cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step, attn
 Prints the CUDA-event time per launch and the algorithmic rate (TFLOP/s or GB/s)."""
@@ -24,7 +25,8 @@ def _case(args, dev):
         dY = (torch.randn((M, N), generator=g, device=dev) * 1e-3).to(torch.bfloat16)
         Y, mask = linear.forward(X, W, b)
         dZ, db = linear.relu_mask_db(dY, mask)
-        dW = torch.empty((N, K), dtype=torch.float32, device=dev)
+        dW = torch.empty((N, K), dtype=torch.bfloat16 if args.dw_dtype == "bf16" else torch.float32,
+                         device=dev)
         dX = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
         fl = 2.0 * M * N * K
         if args.case == "gemm-fwd":
@@ -76,9 +78,13 @@ def main():
     ap.add_argument("--b", type=int, default=8)
     ap.add_argument("--h", type=int, default=32)
     ap.add_argument("--s", type=int, default=8192)
+    ap.add_argument("--variant", type=int, default=0, help="GEMM kernel variant (c3cu_set_gemm_variant)")
+    ap.add_argument("--dw-dtype", choices=["bf16", "fp32"], default="bf16")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    from . import _lib
+    _lib.check(_lib.load().c3cu_set_gemm_variant(args.variant), "c3cu_set_gemm_variant")
     fn, work, unit = _case(args, dev)
     fn()
     torch.cuda.synchronize()
@@ -94,7 +100,7 @@ def main():
     fault_status()
     best, avg = min(times), sum(times) / len(times)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
-    print(json.dumps({"case": args.case, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
+    print(json.dumps({"case": args.case, "variant": args.variant, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
                       "ms_avg": avg, "ms_best": best, "rate_avg": work / (avg * 1e-3) / scale,
                       "rate_best": work / (best * 1e-3) / scale, "unit": unit,
                       "times_ms": [round(t, 4) for t in times]}))
