@@ -1,6 +1,9 @@
 // C-ABI entry points of the tcgen05 GEMM family (include/c3cu.h): the fused
 // Linear+bias+ReLU forward, the dX / dW backward GEMMs and the general bf16 GEMM.
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "gemm2_tcgen05.cuh"
 #include "gemm_tcgen05.cuh"
@@ -18,7 +21,8 @@ using gemm::Params;
 std::atomic<int> g_max_ctas{0};
 
 // Kernel variant: 0 = automatic (the CTA-pair kernel whenever M spans at least two 128-row
-// halves), 1 = single-CTA kernel only, 2 = CTA-pair kernel whenever it applies.
+// halves, with the split-K tail), 1 = single-CTA kernel only, 2 = CTA-pair kernel whenever it
+// applies, without the split-K tail.
 std::atomic<int> g_variant{0};
 
 // Co-resident clusters of two CTAs for a kernel (cached per device and kernel).
@@ -46,6 +50,38 @@ int max_pair_clusters(Kern kern, uint32_t smem_bytes, int threads) {
   }
   cached[dev] = n;
   return n;
+}
+
+// Split-K tail workspace of the CTA-pair kernel, one per (device, stream) so that kernels on
+// different streams never share tickets: fp32 partials for `kSplitMax` split tiles x 2 CTAs
+// x 128 x 256, then per-warp tickets and ready words (zeroed once; every launch leaves them
+// zero).
+constexpr int kSplitMax = 64;
+constexpr size_t kSplitPartialFloats = static_cast<size_t>(kSplitMax) * 2 * gemm2::HM * gemm2::TN;
+constexpr size_t kSplitWords = static_cast<size_t>(kSplitMax) * 2 * 4;
+constexpr size_t kSplitWsBytes = kSplitPartialFloats * 4 + 2 * kSplitWords * 4;
+
+int split_workspace(cudaStream_t stream, float** partial, uint32_t** tickets, uint32_t** ready) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, void*> pool;
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "gemm2: current device");
+  if (rc != C3CU_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  void*& ws = pool[{dev, stream}];
+  if (ws == nullptr) {
+    rc = cuda_status(cudaMalloc(&ws, kSplitWsBytes), "gemm2: split-K workspace");
+    if (rc != C3CU_OK) {
+      ws = nullptr;
+      return rc;
+    }
+    rc = cuda_status(cudaMemset(ws, 0, kSplitWsBytes), "gemm2: clear split-K workspace");
+    if (rc != C3CU_OK) return rc;
+  }
+  *partial = static_cast<float*>(ws);
+  *tickets = reinterpret_cast<uint32_t*>(*partial + kSplitPartialFloats);
+  *ready = *tickets + kSplitWords;
+  return C3CU_OK;
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -79,8 +115,24 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   if (clusters <= 0) clusters = sm_count() / 2;
   const int cap = g_max_ctas.load(std::memory_order_relaxed);
   if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
-  if (tiles < clusters) clusters = tiles;
-  kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, p);
+  // Split-K tail: when the last wave would leave at least half of the clusters idle, its
+  // tiles are computed as two K halves on two clusters each (automatic variant only).
+  Params q = p;
+  q.split_tiles = 0;
+  const int k_blocks = (p.K + gemm2::BK - 1) / gemm2::BK;
+  if (g_variant.load(std::memory_order_relaxed) == 0 && k_blocks >= 8) {
+    const int tail = tiles >= clusters ? tiles % clusters : tiles;
+    if (tail > 0 && 2 * tail <= clusters && tail <= kSplitMax) {
+      q.split_tiles = tail;
+      if (tiles < clusters) clusters = 2 * tiles;
+    }
+  }
+  if (q.split_tiles == 0 && tiles < clusters) clusters = tiles;
+  if (q.split_tiles > 0) {
+    rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
+    if (rc != C3CU_OK) return rc;
+  }
+  kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, q);
   return cuda_status(cudaGetLastError(), "gemm2: launch");
 }
 
@@ -191,6 +243,10 @@ int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ld
   p.bias = bias;
   p.mask = mask;
   p.ldm = ldm;
+  p.split_tiles = 0;
+  p.partial = nullptr;
+  p.tickets = nullptr;
+  p.ready = nullptr;
   const int esize = (epi == kEpiStoreF32 || epi == kEpiBiasStoreF32) ? 4 : 2;
   p.vec_ok = aligned16(out) && ((ldo * esize) % 16 == 0) &&
              (!bias_epi || aligned16(bias)) ? 1 : 0;

@@ -71,6 +71,46 @@ __device__ __forceinline__ void settle_inflight_copies() {
   }
 }
 
+// One unit of a cluster's work: an output tile and the K blocks [kb0, kb1) to accumulate.
+// split >= 0 marks a split-K tail tile (its index among the split tiles).
+struct Item {
+  int tile, kb0, kb1, split;
+};
+
+// Work of cluster `c` of `C`, in order: the full tiles c, c + C, ... below
+// num_tiles - split_tiles (a multiple of C when split_tiles > 0), then, for c < 2 *
+// split_tiles, one K half (c & 1) of split tile c >> 1.
+__device__ __forceinline__ bool work_item(int i, int c, int C, int num_tiles, int split_tiles,
+                                          int k_blocks, Item& it) {
+  const int t_full = num_tiles - split_tiles;
+  const int n_full = t_full > c ? (t_full - c + C - 1) / C : 0;
+  if (i < n_full) {
+    it = Item{c + i * C, 0, k_blocks, -1};
+    return true;
+  }
+  if (split_tiles > 0 && i == n_full && c < 2 * split_tiles) {
+    const int kmid = k_blocks / 2;
+    const bool hi = (c & 1) != 0;
+    it = Item{t_full + (c >> 1), hi ? kmid : 0, hi ? k_blocks : kmid, c >> 1};
+    return true;
+  }
+  return false;
+}
+
+// Bounded acquire-wait for a split partner's "partial published" word.
+__device__ __forceinline__ bool wait_ready(const uint32_t* flag) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t v;
+  while (true) {
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v != 0u) return true;
+    if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS) {
+      record_fault(kFaultWaitPeer, blockIdx.x & 0xffffu);
+      return false;
+    }
+  }
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
@@ -130,10 +170,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       uint32_t armed = 0u, armed_par = 0u;
       bool ok = true;
-      for (int tile = cluster; tile < num_tiles && ok; tile += num_clusters) {
-        const int m0 = (tile / n_tiles) * TM;
-        const int n0 = (tile % n_tiles) * TN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+      Item it;
+      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it);
+           ++i) {
+        const int m0 = (it.tile / n_tiles) * TM;
+        const int n0 = (it.tile % n_tiles) * TN;
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, kFaultWaitEmpty)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&full[s], 2u * STAGE_BYTES);
           const uint32_t bar_leader = mapa_shared(smem_u32(&full[s]), 0u);
@@ -166,11 +208,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       uint32_t acc = 0, acc_ph = 0;
       bool ok = true;
-      for (int tile = cluster; tile < num_tiles && ok; tile += num_clusters) {
+      Item it;
+      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it);
+           ++i) {
         if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, kFaultWaitAccEmpty)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * TN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, kFaultWaitFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
@@ -179,7 +223,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             const uint64_t ad = make_sw128_desc(a_addr + kk * A_KSTEP, A_LBO, 1024);
             const uint64_t bd = make_sw128_desc(b_addr + kk * B_KSTEP, B_LBO, 1024);
-            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb != it.kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty[s], kPairMask);  // frees stage s in both CTAs
           if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -197,13 +241,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const uint32_t q = warp & 3u;
     uint32_t acc = 0, acc_ph = 0;
-    for (int tile = cluster; tile < num_tiles; tile += num_clusters) {
-      const int m0 = (tile / n_tiles) * TM + static_cast<int>(rank) * HM;
-      const int n0 = (tile % n_tiles) * TN;
+    Item it;
+    for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it); ++i) {
+      const int m0 = (it.tile / n_tiles) * TM + static_cast<int>(rank) * HM;
+      const int n0 = (it.tile % n_tiles) * TN;
       if (!mbar_wait(&acc_full[acc], acc_ph, kFaultWaitAccFull)) break;
       tc_fence_after();
       const int row = m0 + static_cast<int>(q * 32 + lane);
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * TN;
+      // Split-K tail: per warp (32 rows) a ticket decides which K half publishes its fp32
+      // partial and which one adds it and runs the epilogue. The adder waits only for a
+      // partner that already holds its ticket, i.e. is past its main loop.
+      bool split = it.split >= 0, adder = false;
+      uint32_t word = 0;
+      float* part = nullptr;
+      if (split) {
+        const uint32_t slot = static_cast<uint32_t>(it.split) * 2u + rank;
+        word = slot * 4u + q;
+        part = p.partial + static_cast<size_t>(slot) * (HM * TN) + q * 32u + lane;
+        uint32_t t = 0;
+        if (lane == 0) t = atomicAdd(&p.tickets[word], 1u);
+        adder = __shfl_sync(0xffffffffu, t, 0) != 0u;
+        if (adder) {
+          uint32_t ok = 1;
+          if (lane == 0) ok = wait_ready(&p.ready[word]) ? 1u : 0u;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          uint32_t v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&p.ready[word]) : "memory");
+          (void)v;
+          if (!ok) part = nullptr;  // partner never published: fault recorded, no add
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < TN / 32; ++c) {
         const int col0 = n0 + c * 32;
@@ -211,7 +279,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_wait_ld();
+        if (split && !adder) {
+          // partial[col][row] inside the slot: a warp stores 128 contiguous bytes per column
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(part + (c * 32 + j) * HM, __uint_as_float(r[j]));
+          continue;
+        }
+        if (split && part != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __ldcg(part + (c * 32 + j) * HM)));
+        }
         gemm::epilogue_chunk<EPI>(p, r, row, col0);
+      }
+      if (split) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+          if (!adder) {
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&p.ready[word]), "r"(1u) : "memory");
+          } else {
+            // both halves are done with the words: leave them zero for the next launch
+            p.ready[word] = 0u;
+            p.tickets[word] = 0u;
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();

@@ -124,10 +124,12 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
  * default). A host that overlaps a collective with a GEMM lowers it to leave SMs free. */
 int c3cu_set_gemm_max_ctas(int max_ctas);
 /* GEMM kernel variant for the calls that follow (process-wide): 0 = automatic (the CTA-pair
- * kernel, 256 x 256 tiles on two SMs with cta_group::2, whenever M > 128; else the single-CTA
- * 128 x 256 kernel), 1 = single-CTA kernel only, 2 = CTA-pair kernel wherever it applies.
- * Results are identical in every variant up to fp32 summation order, which is the same
- * sequential-k order in both kernels. */
+ * kernel, 256 x 256 tiles on two SMs with cta_group::2, whenever M > 128, else the single-CTA
+ * 128 x 256 kernel; when the last wave of tiles would leave half of the SM pairs idle, its
+ * tiles are split in two K halves whose fp32 partial sums are added once, K-half order
+ * fixed), 1 = single-CTA kernel only, 2 = CTA-pair kernel without the K split. Variants 1
+ * and 2 give identical bits (the same K order); on split tiles variant 0 accumulates the two
+ * K halves separately, so it differs from them within the fp32 accumulation error bound. */
 int c3cu_set_gemm_variant(int variant);
 
 /* ------------------------------------------------------------------ exact fp32 (CUDA cores)

@@ -216,22 +216,46 @@ def gemm_variant():
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 520, 1000), (517, 1032, 776),
-                                   (1024, 768, 4096), (129, 256, 64)])
-def test_pair_kernel_matches_single_cta_kernel(cuda_device, gemm_variant, M, N, K):
-    """The CTA-pair kernel (256 x 256 tiles, cta_group::2) and the single-CTA kernel give the
-    same bits: both accumulate each output in the same sequential K order."""
+                                   (1024, 768, 4096), (129, 256, 64), (4096, 512, 1024)])
+def test_gemm_variants_agree(cuda_device, gemm_variant, M, N, K):
+    """Variant 1 (single-CTA kernel) and variant 2 (CTA-pair kernel) give the same bits: both
+    accumulate each output in the same sequential K order. Variant 0 (pair kernel + split-K
+    tail; (4096, 512, 1024) splits the forward and dW tiles) sums the two K halves separately
+    and adds them, so its fp32 results differ within the fp32 accumulation error bound
+    (relative to the sum of |terms|) and its bf16 results by at most one rounding."""
     X, W, b = _fwd_inputs(M, N, K, 7 + M, cuda_device)
     dY = randn((M, N), 0.01, 8 + M).to(cuda_device)
     outs = {}
-    for v in (1, 2):
+    gemm_variant(1)
+    _, mask1 = linear.forward(X, W, b, "nk")
+    dZ, _ = linear.relu_mask_db(dY, mask1)  # one dZ for every variant: a ReLU-boundary mask
+    for v in (1, 2, 0):                     # flip would change dZ by a whole dY element
         gemm_variant(v)
         Y, mask = linear.forward(X, W, b, "nk")
-        dZ, db = linear.relu_mask_db(dY, mask)
         dX = linear.grad_input(dZ, W, "nk")
         dW = linear.grad_weight(dZ, X, "nk")
         dWb = linear.grad_weight(dZ, X, "nk", out_dtype=torch.bfloat16)
         dWkn = linear.grad_weight(dZ, X, "kn")
         torch.cuda.synchronize()
         outs[v] = [t.cpu() for t in (Y, mask, dX, dW, dWb, dWkn)]
-    for name, a, c in zip(("Y", "mask", "dX", "dW", "dW_bf16", "dW_kn"), outs[1], outs[2]):
+    names = ("Y", "mask", "dX", "dW", "dW_bf16", "dW_kn")
+    for name, a, c in zip(names, outs[1], outs[2]):
         assert torch.equal(a, c), f"{name} differs between the kernels at {M}x{N}x{K}"
+    Y1, m1, dX1, dW1, dWb1, dWkn1 = outs[1]
+    Y0, m0, dX0, dW0, dWb0, dWkn0 = outs[0]
+    absprod = (f32(dZ).__abs__().T @ np.abs(f32(X)))  # sum of |terms| of each dW element
+    for name, a, c, s_ in (("dW", dW0, dW1, absprod), ("dW_kn", dWkn0, dWkn1, absprod.T)):
+        assert ((a - c).abs().numpy() <= 2e-6 * s_ + 1e-30).all(), name
+    # bf16 outputs: one rounding of a slightly different fp32 value, so at most one bf16 ulp
+    # apart, or both within the fp32 summation error of zero (a ReLU output at the boundary)
+    for name, a, c in (("Y", Y0, Y1), ("dX", dX0, dX1), ("dW_bf16", dWb0, dWb1)):
+        a, c = a.float(), c.float()
+        bound = 2.0 ** -7 * torch.maximum(a.abs(), c.abs()) + 1e-5 * c.abs().max()
+        assert ((a - c).abs() <= bound).all(), f"{name}: more than one bf16 ulp"
+    # ReLU mask bits can differ only where the pre-activation rounds to about zero
+    b0 = unpack_mask(m0.numpy().view(np.uint32), N)
+    b1 = unpack_mask(m1.numpy().view(np.uint32), N)
+    diff = b0 != b1
+    if diff.any():
+        y = np.maximum(np.abs(f32(Y0)), np.abs(f32(Y1)))[diff]
+        assert y.max() <= 1e-4 * float(np.abs(f32(Y1)).max()), "mask flip away from zero"
