@@ -83,7 +83,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.05)
+            self._stop.wait(0.01)
 
     def __enter__(self):
         if self._nv is not None:
@@ -321,7 +321,7 @@ def run_c3(args):
                                      "none": "none"}[collective]},
             "frac_of_peak": value / world / peak,
             "kernel_ms": ktime,
-            "roofline": {"bound": "tensor", "kernel": "c3cu::gemm::gemm_kernel (fwd+dW+dX)",
+            "roofline": {"bound": "tensor", "kernel": "c3cu::gemm2::gemm2_kernel (CTA pair; fwd+dW+dX)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} {'sustained' if long_region else 'burst'}",

@@ -30,7 +30,7 @@ constexpr int TN = 256;          // output tile columns per pair
 constexpr int HM = TM / 2;       // A rows per CTA
 constexpr int HN = TN / 2;       // B rows (output columns) loaded per CTA
 constexpr int BK = 64;
-constexpr int STAGES = 6;
+constexpr int STAGES = 7;
 constexpr int UMMA_K = 16;
 constexpr int kThreads = 192;
 constexpr uint32_t A_STAGE_BYTES = HM * BK * 2;  // 16 KiB
