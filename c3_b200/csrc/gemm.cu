@@ -52,13 +52,13 @@ int max_pair_clusters(Kern kern, uint32_t smem_bytes, int threads) {
   return n;
 }
 
-// Split-K tail workspace of the CTA-pair kernel, one per (device, stream) so that kernels on
-// different streams never share tickets: fp32 partials for `kSplitMax` split tiles x 2 CTAs
-// x 128 x 256, then per-warp tickets and ready words (zeroed once; every launch leaves them
-// zero).
-constexpr int kSplitMax = 64;
+// Split-tile workspace of the CTA-pair kernel, one per (device, stream) so that kernels on
+// different streams never share tickets: fp32 partials for `kSplitMax` shared tiles x 2 CTAs
+// x 128 x 256 (a slot per cluster boundary, at most one per cluster), then per-warp tickets
+// and ready words (zeroed once; every launch leaves them zero).
+constexpr int kSplitMax = 80;
 constexpr size_t kSplitPartialFloats = static_cast<size_t>(kSplitMax) * 2 * gemm2::HM * gemm2::TN;
-constexpr size_t kSplitWords = static_cast<size_t>(kSplitMax) * 2 * 4;
+constexpr size_t kSplitWords = static_cast<size_t>(kSplitMax) * 2 * gemm2::kEpiWarps;
 constexpr size_t kSplitWsBytes = kSplitPartialFloats * 4 + 2 * kSplitWords * 4;
 
 int split_workspace(cudaStream_t stream, float** partial, uint32_t** tickets, uint32_t** ready) {
@@ -115,22 +115,33 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   if (clusters <= 0) clusters = sm_count() / 2;
   const int cap = g_max_ctas.load(std::memory_order_relaxed);
   if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
-  // Split-K tail: when the last wave would leave at least half of the clusters idle, its
-  // tiles are computed as two K halves on two clusters each (automatic variant only).
+  // Split-K tail (automatic variant only, K at least 64 blocks): when the last wave would
+  // leave at least half of the clusters idle, its tiles run as two K halves on two clusters
+  // each. With shorter K the fp32 partial exchange costs about as much as a half's main loop
+  // (measured: dW with K = 2048 ran 5% slower split).
+  // (A stream-K split of the last waves balanced the clusters exactly but ran slower: the
+  // shorter pieces and their fix-ups left the tensor pipe waiting on the epilogue.)
   Params q = p;
-  q.split_tiles = 0;
+  q.sk_mode = 0;
+  q.sk_first = 0;
   const int k_blocks = (p.K + gemm2::BK - 1) / gemm2::BK;
-  if (g_variant.load(std::memory_order_relaxed) == 0 && k_blocks >= 8) {
-    const int tail = tiles >= clusters ? tiles % clusters : tiles;
-    if (tail > 0 && 2 * tail <= clusters && tail <= kSplitMax) {
-      q.split_tiles = tail;
+  if (g_variant.load(std::memory_order_relaxed) == 0 && k_blocks >= 64) {
+    const int tail = tiles % clusters;
+    if (tail > 0 && 2 * tail <= clusters) {
+      q.sk_mode = 1;
+      q.sk_first = tiles - tail;
       if (tiles < clusters) clusters = 2 * tiles;
     }
   }
-  if (q.split_tiles == 0 && tiles < clusters) clusters = tiles;
-  if (q.split_tiles > 0) {
-    rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
-    if (rc != C3CU_OK) return rc;
+  if (q.sk_mode == 0 && tiles < clusters) clusters = tiles;
+  if (q.sk_mode != 0) {
+    if (clusters > kSplitMax) {
+      q.sk_mode = 0;  // more boundary slots than the workspace holds: whole tiles
+      if (tiles < clusters) clusters = tiles;
+    } else {
+      rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
+      if (rc != C3CU_OK) return rc;
+    }
   }
   kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, q);
   return cuda_status(cudaGetLastError(), "gemm2: launch");
@@ -243,7 +254,8 @@ int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ld
   p.bias = bias;
   p.mask = mask;
   p.ldm = ldm;
-  p.split_tiles = 0;
+  p.sk_mode = 0;
+  p.sk_first = 0;
   p.partial = nullptr;
   p.tickets = nullptr;
   p.ready = nullptr;

@@ -15,8 +15,10 @@
 //               `full` barrier (the leader arms it with the bytes of both halves).
 //   warp 1      TMEM owner (pair allocation); in the leader also the MMA issuer. Each
 //               stage is released in both CTAs by one multicast tcgen05.commit.
-//   warps 2..5  epilogue on this CTA's 128 accumulator rows; they release an accumulator
-//               by arriving on the leader's `acc_empty` barrier (8 arrivals: both CTAs).
+//   warps 2..9  epilogue on this CTA's 128 accumulator rows, two warps per TMEM lane
+//               quarter (warp w reads lanes 32 * (w % 4) ...), each on half of the 256
+//               columns; they release an accumulator by arriving on the leader's
+//               `acc_empty` barrier (16 arrivals: both CTAs).
 // Loads use no cluster multicast: every CTA reads its own operands from global memory.
 #pragma once
 
@@ -32,7 +34,8 @@ constexpr int HN = TN / 2;       // B rows (output columns) loaded per CTA
 constexpr int BK = 64;
 constexpr int STAGES = 7;
 constexpr int UMMA_K = 16;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t A_STAGE_BYTES = HM * BK * 2;  // 16 KiB
 constexpr uint32_t B_STAGE_BYTES = HN * BK * 2;  // 16 KiB
 constexpr uint32_t STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
@@ -72,29 +75,29 @@ __device__ __forceinline__ void settle_inflight_copies() {
 }
 
 // One unit of a cluster's work: an output tile and the K blocks [kb0, kb1) to accumulate.
-// split >= 0 marks a split-K tail tile (its index among the split tiles).
+// split >= 0 marks a tile that two clusters share as two K halves (the index of its fp32
+// partial slot); the two halves meet through a ticket in the epilogue.
 struct Item {
   int tile, kb0, kb1, split;
 };
 
-// Work of cluster `c` of `C`, in order: the full tiles c, c + C, ... below
-// num_tiles - split_tiles (a multiple of C when split_tiles > 0), then, for c < 2 *
-// split_tiles, one K half (c & 1) of split tile c >> 1.
-__device__ __forceinline__ bool work_item(int i, int c, int C, int num_tiles, int split_tiles,
-                                          int k_blocks, Item& it) {
-  const int t_full = num_tiles - split_tiles;
-  const int n_full = t_full > c ? (t_full - c + C - 1) / C : 0;
-  if (i < n_full) {
+// Work of cluster `c` of `C`: the tiles c, c + C, ... below sk_first (whole waves; all
+// tiles when sk_mode is 0), then, with sk_mode 1, K half (c & 1) of tail tile
+// sk_first + (c >> 1) for c < 2 * (num_tiles - sk_first). The host uses the tail split when
+// the last wave would leave at least half of the clusters idle.
+__device__ __forceinline__ bool work_item(int i, int c, int C, int num_tiles, int sk_mode,
+                                          int sk_first, int k_blocks, Item& it) {
+  const int t_dp = sk_mode == 1 ? sk_first : num_tiles;
+  const int n_dp = t_dp > c ? (t_dp - c + C - 1) / C : 0;
+  if (i < n_dp) {
     it = Item{c + i * C, 0, k_blocks, -1};
     return true;
   }
-  if (split_tiles > 0 && i == n_full && c < 2 * split_tiles) {
-    const int kmid = k_blocks / 2;
-    const bool hi = (c & 1) != 0;
-    it = Item{t_full + (c >> 1), hi ? kmid : 0, hi ? k_blocks : kmid, c >> 1};
-    return true;
-  }
-  return false;
+  if (sk_mode != 1 || i != n_dp || c >= 2 * (num_tiles - t_dp)) return false;
+  const int kmid = k_blocks / 2;
+  const bool hi = (c & 1) != 0;
+  it = Item{t_dp + (c >> 1), hi ? kmid : 0, hi ? k_blocks : kmid, c >> 1};
+  return true;
 }
 
 // Bounded acquire-wait for a split partner's "partial published" word.
@@ -147,7 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);  // one arrival per epilogue warp of both CTAs
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
     fence_mbarrier_init();
@@ -171,7 +174,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t armed = 0u, armed_par = 0u;
       bool ok = true;
       Item it;
-      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it);
+      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it);
            ++i) {
         const int m0 = (it.tile / n_tiles) * TM;
         const int n0 = (it.tile % n_tiles) * TN;
@@ -209,7 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t acc = 0, acc_ph = 0;
       bool ok = true;
       Item it;
-      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it);
+      for (int i = 0; ok && work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it);
            ++i) {
         if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, kFaultWaitAccEmpty)) { ok = false; break; }
         tc_fence_after();
@@ -238,11 +241,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const uint32_t q = warp & 3u;
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const uint32_t q = warp & 3u;                 // TMEM lane quarter
+    const uint32_t ew = warp - 2u;                // epilogue warp 0..7
+    const int c_lo = static_cast<int>(ew >> 2) * (TN / 64);  // first of this warp's 4 chunks
     uint32_t acc = 0, acc_ph = 0;
     Item it;
-    for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.split_tiles, k_blocks, it); ++i) {
+    for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it); ++i) {
       const int m0 = (it.tile / n_tiles) * TM + static_cast<int>(rank) * HM;
       const int n0 = (it.tile % n_tiles) * TN;
       if (!mbar_wait(&acc_full[acc], acc_ph, kFaultWaitAccFull)) break;
@@ -257,7 +262,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       float* part = nullptr;
       if (split) {
         const uint32_t slot = static_cast<uint32_t>(it.split) * 2u + rank;
-        word = slot * 4u + q;
+        word = slot * kEpiWarps + ew;
         part = p.partial + static_cast<size_t>(slot) * (HM * TN) + q * 32u + lane;
         uint32_t t = 0;
         if (lane == 0) t = atomicAdd(&p.tickets[word], 1u);
@@ -273,7 +278,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
 #pragma unroll 1
-      for (int c = 0; c < TN / 32; ++c) {
+      for (int c = c_lo; c < c_lo + TN / 64; ++c) {
         const int col0 = n0 + c * 32;
         if (col0 >= p.N) break;
         uint32_t r[32];

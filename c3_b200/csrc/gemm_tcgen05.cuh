@@ -57,11 +57,14 @@ struct Params {
   uint32_t* mask;        // [M][ldm] bit-packed ReLU mask (kEpiBiasReluMask)
   int64_t ldm;           // mask row stride, 32-bit words
   int32_t vec_ok;        // 1 when every 32-column chunk may use 16-byte stores
-  // Split-K tail of the CTA-pair kernel (0 = none): the last `split_tiles` tiles are computed
-  // as two K halves by two clusters; the half that finishes second adds the other's partial
-  // (fp32, `partial`) before its epilogue. `tickets` / `ready` are per-warp words that the
-  // second half returns to zero, so the workspace is ready for the next launch.
-  int32_t split_tiles;
+  // Work split of the CTA-pair kernel (sk_mode 0 = round robin over whole tiles; 1 = round
+  // robin over the first sk_first tiles, then every remaining tile as two K halves on two
+  // clusters). A tile shared by two clusters is finished by the half that takes the second
+  // ticket: it adds the other half's fp32 partial (`partial`) before its epilogue.
+  // `tickets` / `ready` are per-warp words that the second half returns to zero, so the
+  // workspace is ready for the next launch.
+  int32_t sk_mode;
+  int32_t sk_first;
   float* partial;
   uint32_t* tickets;
   uint32_t* ready;

@@ -216,13 +216,15 @@ def gemm_variant():
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 520, 1000), (517, 1032, 776),
-                                   (1024, 768, 4096), (129, 256, 64), (4096, 512, 1024)])
+                                   (1024, 768, 4096), (129, 256, 64), (4096, 512, 4096),
+                                   (8192, 2560, 4096)])
 def test_gemm_variants_agree(cuda_device, gemm_variant, M, N, K):
     """Variant 1 (single-CTA kernel) and variant 2 (CTA-pair kernel) give the same bits: both
-    accumulate each output in the same sequential K order. Variant 0 (pair kernel + split-K
-    tail; (4096, 512, 1024) splits the forward and dW tiles) sums the two K halves separately
-    and adds them, so its fp32 results differ within the fp32 accumulation error bound
-    (relative to the sum of |terms|) and its bf16 results by at most one rounding."""
+    accumulate each output in the same sequential K order. Variant 0 (pair kernel with the
+    split-K tail: (4096, 512, 4096) halves every forward and dW tile, (8192, 2560, 4096) the
+    forward's last-wave tiles) sums the two K halves of a split tile separately and adds them,
+    so its fp32 results differ within the fp32 accumulation error bound (relative to the sum
+    of |terms|) and its bf16 results by at most one rounding."""
     X, W, b = _fwd_inputs(M, N, K, 7 + M, cuda_device)
     dY = randn((M, N), 0.01, 8 + M).to(cuda_device)
     outs = {}
