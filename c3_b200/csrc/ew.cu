@@ -198,9 +198,39 @@ size_t colsum_workspace(int64_t M, int64_t N) {
   return ((partial_bytes + 255u) & ~static_cast<size_t>(255u)) + ticket_bytes;
 }
 
+// Strip tickets owned by the library, one array per (device, stream), zeroed once when it
+// is created. Every launch leaves its tickets at zero (the last block of a strip re-arms
+// its ticket), so launches on the stream need no clearing pass of their own; launches on
+// different streams never share an array.
+constexpr int64_t kPoolStrips = 1 << 16;
+
+int ticket_pool(cudaStream_t st, unsigned int** out) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, cudaStream_t>, void*>> pool;
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "column sum: current device");
+  if (rc != C3CU_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : pool)
+    if (e.first.first == dev && e.first.second == st) {
+      *out = static_cast<unsigned int*>(e.second);
+      return C3CU_OK;
+    }
+  void* p = nullptr;
+  rc = cuda_status(cudaMalloc(&p, kPoolStrips * 4), "column sum: ticket array");
+  if (rc != C3CU_OK) return rc;
+  rc = cuda_status(cudaMemset(p, 0, kPoolStrips * 4), "column sum: clear ticket array");
+  if (rc != C3CU_OK) return rc;
+  pool.push_back({{dev, st}, p});
+  *out = static_cast<unsigned int*>(p);
+  return C3CU_OK;
+}
+
+// `pooled`: take the strip tickets from the library's per-stream array (no clearing pass);
+// otherwise they live in the caller's workspace and are cleared before the kernel.
 template <bool MASKED>
 int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, int64_t M, int64_t N,
-                  void* ws, size_t ws_bytes, cudaStream_t st) {
+                  void* ws, size_t ws_bytes, cudaStream_t st, bool pooled = true) {
   if (M < 0 || N < 0 || M > INT32_MAX || N > INT32_MAX) {
     set_error("column sum: sizes out of range");
     return C3CU_ERR_INVALID;
@@ -230,8 +260,13 @@ int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, in
   const size_t partial_bytes = static_cast<size_t>(rbs) * static_cast<size_t>(N) * 4u;
   unsigned int* tickets = reinterpret_cast<unsigned int*>(
       static_cast<uint8_t*>(ws) + ((partial_bytes + 255u) & ~static_cast<size_t>(255u)));
-  int rc = cuda_status(cudaMemsetAsync(tickets, 0, static_cast<size_t>(strips) * 4u, st),
-                       "column sum: reset tickets");
+  int rc = C3CU_OK;
+  if (pooled && strips <= kPoolStrips) {
+    rc = ticket_pool(st, &tickets);
+  } else {
+    rc = cuda_status(cudaMemsetAsync(tickets, 0, static_cast<size_t>(strips) * 4u, st),
+                     "column sum: reset tickets");
+  }
   if (rc != C3CU_OK) return rc;
   const int esize = MASKED ? 2 : 4;
   const int vec_ok = aligned16(in) && (!MASKED || aligned16(dz)) && ((N * esize) % 16 == 0);
@@ -468,7 +503,7 @@ int c3cu_relu_mask_db_noalloc(const void* dY, const uint32_t* mask, void* dZ, fl
   // launch_colsum clears the ticket counters in the scratch before the kernel; the partial
   // sums are fully written before they are read, so stale contents from earlier calls are harmless.
   return c3cu::ew::launch_colsum<true>(dY, mask, dZ, db, M, N, scratch, C3CU_NOALLOC_SCRATCH_BYTES,
-                                       static_cast<cudaStream_t>(stream));
+                                       static_cast<cudaStream_t>(stream), /*pooled=*/false);
 }
 
 size_t c3cu_sum_rows_f32_workspace(int64_t M, int64_t N) { return c3cu::ew::colsum_workspace(M, N); }
