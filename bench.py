@@ -206,7 +206,7 @@ def run_c3(args):
                                 device_id=dev)
 
     import c3_b200
-    from c3_b200.data_parallel import LinearReluTrainStep, env_grad_dtype, shard_rows
+    from c3_b200.data_parallel import LinearReluTrainStep, default_overlap, env_grad_dtype, shard_rows
     c3_b200.load()
     c3_b200.device_check()
 
@@ -232,10 +232,11 @@ def run_c3(args):
     # all-reduce starts on the comm stream as soon as its GEMM ends (the last band carries
     # db). `reserve` SMs are left to the collective while the dX GEMM overlaps it.
     chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "1")))
-    reserve = int(os.environ.get("C3_BENCH_AR_SMS", "0")) if world > 1 else 0
+    ar_ctas, ar_sms = default_overlap(world)
+    reserve = int(os.environ.get("C3_BENCH_AR_SMS", str(ar_sms))) if world > 1 else 0
     train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
                                 collective="auto" if ar_env == "nvls" else ar_env,
-                                chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", "16")),
+                                chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", str(ar_ctas))),
                                 reserve_sms=reserve)
     chunks = len(train.bands)
     collective = "none" if world == 1 else train.sync.collective
