@@ -13,6 +13,8 @@
 //               the S buffer; O is rescaled in TMEM only when the running maximum grows by
 //               more than 2^8 (lazy rescaling), and normalised by the row sum at the end
 // TMEM: S buffers at columns [0,128) and [128,256), O at [256,384) (512 allocated).
+// The default launch is flash_fwd2_kernel (attn2.cuh): two query tiles per CTA sharing each
+// K / V block, with ping-pong softmax warpgroups; this single-tile kernel is variant 1.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -342,6 +344,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace attn
+}  // namespace c3cu
+
+#include "attn2.cuh"
+
+namespace c3cu {
+namespace attn {
+
+// 0 = automatic (two query tiles per CTA), 1 = one query tile per CTA.
+static int g_attn_variant = 0;
+
 namespace {
 int encode_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S) {
   if (!aligned16(base)) {
@@ -412,20 +425,47 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
   p.causal = causal ? 1 : 0;
   p.O = static_cast<__nv_bfloat16*>(O);
   p.lse = LSE;
-  static bool attr = false;
-  if (!attr) {
-    rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          attn::SMEM_BYTES),
+  if (attn::g_attn_variant == 1) {
+    static bool attr = false;
+    if (!attr) {
+      rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            attn::SMEM_BYTES),
+                       "flash_attn_fwd: set shared memory");
+      if (rc != C3CU_OK) return rc;
+      attr = true;
+    }
+    const int64_t grid = static_cast<int64_t>(p.BH) * p.q_tiles;
+    if (grid > INT32_MAX) {
+      set_error("flash_attn_fwd: grid too large");
+      return C3CU_ERR_INVALID;
+    }
+    attn::flash_fwd_kernel<<<static_cast<unsigned>(grid), attn::kThreads, attn::SMEM_BYTES,
+                             static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+    return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+  }
+  static bool attr2 = false;
+  if (!attr2) {
+    rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          attn::SMEM_BYTES2),
                      "flash_attn_fwd: set shared memory");
     if (rc != C3CU_OK) return rc;
-    attr = true;
+    attr2 = true;
   }
-  const int64_t grid = static_cast<int64_t>(p.BH) * p.q_tiles;
+  const int64_t grid = static_cast<int64_t>(p.BH) * ((p.q_tiles + 1) / 2);
   if (grid > INT32_MAX) {
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
-  attn::flash_fwd_kernel<<<static_cast<unsigned>(grid), attn::kThreads, attn::SMEM_BYTES,
-                           static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  attn::flash_fwd2_kernel<<<static_cast<unsigned>(grid), attn::kThreads2, attn::SMEM_BYTES2,
+                            static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+}
+
+extern "C" int c3cu_set_attn_variant(int variant) {
+  if (variant < 0 || variant > 1) {
+    c3cu::set_error("set_attn_variant: unknown variant %d", variant);
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::attn::g_attn_variant = variant;
+  return C3CU_OK;
 }

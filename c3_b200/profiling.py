@@ -80,11 +80,13 @@ def main():
     ap.add_argument("--s", type=int, default=8192)
     ap.add_argument("--variant", type=int, default=0, help="GEMM kernel variant (c3cu_set_gemm_variant)")
     ap.add_argument("--dw-dtype", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--attn-variant", type=int, default=0, help="c3cu_set_attn_variant")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     from . import _lib
     _lib.check(_lib.load().c3cu_set_gemm_variant(args.variant), "c3cu_set_gemm_variant")
+    _lib.check(_lib.load().c3cu_set_attn_variant(args.attn_variant), "c3cu_set_attn_variant")
     fn, work, unit = _case(args, dev)
     fn()
     torch.cuda.synchronize()
@@ -100,7 +102,7 @@ def main():
     fault_status()
     best, avg = min(times), sum(times) / len(times)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
-    print(json.dumps({"case": args.case, "variant": args.variant, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
+    print(json.dumps({"case": args.case, "variant": args.variant, "attn_variant": args.attn_variant, "m": args.m, "n": args.n, "k": args.k, "elems": args.elems,
                       "ms_avg": avg, "ms_best": best, "rate_avg": work / (avg * 1e-3) / scale,
                       "rate_best": work / (best * 1e-3) / scale, "unit": unit,
                       "times_ms": [round(t, 4) for t in times]}))

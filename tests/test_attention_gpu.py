@@ -62,3 +62,23 @@ def test_flash_attention_cfg5_full_size_sampled(cuda_device):
     assert torch.isfinite(O.float()).all()
     for (b, h, r0) in [(0, 0, 0), (7, 31, S - 64), (3, 17, 4000), (5, 2, 8128 - 700)]:
         _check(Q, K, V, O, L, True, [(b, h)], rows_per_pair=(r0, r0 + 64))
+
+
+@pytest.mark.parametrize("S,causal", [(384, True), (1024, True), (300, False)])
+def test_flash_attention_kernels_agree(cuda_device, S, causal):
+    """The two-tile kernel (default) and the one-tile kernel (variant 1) agree to bf16
+    rounding: they differ only in the exponentials computed on the FMA pipe (relative error
+    below 1e-4) and the resulting bf16 roundings of P and O."""
+    from c3_b200 import _lib
+    L = _lib.load()
+    Q, K, V = _qkv(1, 4, S, 77 + S, cuda_device)
+    try:
+        _lib.check(L.c3cu_set_attn_variant(1), "c3cu_set_attn_variant")
+        O1, L1 = flash_attn_fwd(Q, K, V, causal=causal)
+        _lib.check(L.c3cu_set_attn_variant(0), "c3cu_set_attn_variant")
+        O0, L0 = flash_attn_fwd(Q, K, V, causal=causal)
+        torch.cuda.synchronize()
+    finally:
+        L.c3cu_set_attn_variant(0)
+    assert_bf16_close(O0.float().cpu().numpy(), O1.float().cpu().numpy(), "O two-tile vs one-tile")
+    assert (L0 - L1).abs().max().item() <= 1e-3
