@@ -443,22 +443,21 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
                              static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
     return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
   }
-  static bool attr2 = false;
-  if (!attr2) {
-    rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          attn::SMEM_BYTES2),
-                     "flash_attn_fwd: set shared memory");
-    if (rc != C3CU_OK) return rc;
-    attr2 = true;
-  }
   const int64_t grid = static_cast<int64_t>(p.BH) * ((p.q_tiles + 1) / 2);
   if (grid > INT32_MAX) {
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
-  attn::flash_fwd2_kernel<<<static_cast<unsigned>(grid), attn::kThreads2, attn::SMEM_BYTES2,
-                            static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+  auto go = [&](auto kern) -> int {
+    int r = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             attn::SMEM_BYTES2),
+                        "flash_attn_fwd: set shared memory");
+    if (r != C3CU_OK) return r;
+    kern<<<static_cast<unsigned>(grid), attn::kThreads2, attn::SMEM_BYTES2,
+           static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+    return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+  };
+  return go(attn::flash_fwd2_kernel);
 }
 
 extern "C" int c3cu_set_attn_variant(int variant) {

@@ -15,11 +15,12 @@
 // PV_t,j, which reads P_t,j from the same columns; tcgen05.mma operations of one thread
 // execute in issue order, so the read precedes the overwrite.
 //
-// Exponentials: with D = 128 the MUFU ex2 rate (16 per clock per SM) equals the score rate of
-// the tensor pipe, so part of each 32-score chunk is computed on the FMA pipe instead:
-// 2^x = 2^floor(x) * p(x - floor(x)) with a degree-3 polynomial p fitted here to 2^f on
-// [0, 1) (weighted least squares on Chebyshev nodes; max relative error 7.5e-5, far below
-// the bf16 rounding of P, 2^-9).
+// Exponentials all use ex2.approx (MUFU). Moving part of each 32-score chunk to the FMA
+// pipe (2^floor(x) times a degree-3 polynomial) measured slower at every fraction tried
+// (6, 10, 14, 18 of 32): the softmax is bound by its instruction stream, not by MUFU.
+// With 10 warps a sub-partition holds three of them, so its 16K registers cap a thread at
+// 168; the 128 scores of a row stay in registers (a three-input max.f32 row maximum made the
+// kernel spill at that cap).
 #pragma once
 
 namespace c3cu {
@@ -29,18 +30,7 @@ constexpr int kThreads2 = 320;
 constexpr int KV_STAGES2 = 2;
 // smem: Q0 | Q1 | K0 V0 | K1 V1 | barriers
 constexpr uint32_t SMEM_BYTES2 = TILE_BYTES * (2 + 2 * KV_STAGES2) + 16 * 8 + 1024;
-constexpr int kPolyPerChunk = 10;  // scores of each 32-score chunk exponentiated on the FMA pipe
 
-__device__ __forceinline__ float exp2_fma(float x) {
-  constexpr float c0 = 0.9999252557754517f, c1 = 0.6958334445953369f;
-  constexpr float c2 = 0.2260674387216568f, c3 = 0.07802435755729675f;
-  const float xc = fmaxf(x, -127.f);
-  const float fi = floorf(xc);
-  const float f = xc - fi;
-  const float p = fmaf(fmaf(fmaf(c3, f, c2), f, c1), f, c0);
-  const float r = __int_as_float(__float_as_int(p) + (static_cast<int>(fi) << 23));
-  return x < -126.f ? 0.f : r;
-}
 
 __global__ void __launch_bounds__(kThreads2, 1)
     flash_fwd2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
@@ -250,12 +240,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         for (int i = 0; i < 16; ++i) {
           float2 x = make_float2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
           x = ffma2(x, sc2, nb2);
-          float2 e;
-          if (2 * i >= 32 - kPolyPerChunk) {
-            e = make_float2(exp2_fma(x.x), exp2_fma(x.y));
-          } else {
-            e = make_float2(ex2(x.x), ex2(x.y));
-          }
+          const float2 e = make_float2(ex2(x.x), ex2(x.y));
           rs2 = fadd2(rs2, e);
           w[i] = pack_bf16x2(e.x, e.y);
         }
