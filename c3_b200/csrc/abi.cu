@@ -18,6 +18,8 @@ int c3cu_fault_get_attn(uint32_t* out);
 int c3cu_fault_clear_attn();
 int c3cu_fault_get_nvls(uint32_t* out);
 int c3cu_fault_clear_nvls();
+int c3cu_fault_get_train(uint32_t* out);
+int c3cu_fault_clear_train();
 
 namespace c3cu {
 
@@ -136,9 +138,10 @@ int c3cu_fault_status(uint32_t* code) {
   *code = 0u;
   int rc = c3cu::cuda_status(cudaDeviceSynchronize(), "c3cu_fault_status: synchronize");
   if (rc != C3CU_OK) return rc;
-  uint32_t words[4] = {0u, 0u, 0u, 0u};
+  uint32_t words[5] = {0u, 0u, 0u, 0u, 0u};
   if (c3cu_fault_get_gemm(&words[0]) || c3cu_fault_get_ew(&words[1]) ||
-      c3cu_fault_get_attn(&words[2]) || c3cu_fault_get_nvls(&words[3])) {
+      c3cu_fault_get_attn(&words[2]) || c3cu_fault_get_nvls(&words[3]) ||
+      c3cu_fault_get_train(&words[4])) {
     c3cu::set_error("c3cu_fault_status: reading fault words failed");
     return C3CU_ERR_CUDA;
   }
@@ -148,6 +151,7 @@ int c3cu_fault_status(uint32_t* code) {
   c3cu_fault_clear_ew();
   c3cu_fault_clear_attn();
   c3cu_fault_clear_nvls();
+  c3cu_fault_clear_train();
   if (*code != 0u) {
     c3cu::set_error("kernel fault recorded: code %u (site %u)", *code & 0xffffu, *code >> 16);
     return C3CU_ERR_FAULT;

@@ -16,7 +16,11 @@
 namespace c3cu {
 namespace exact {
 
-constexpr int TM = 64, TN = 64, TK = 16;  // block tile; 256 threads, 4x4 outputs each
+constexpr int TK = 16;  // k depth of one shared-memory stage
+// Block tile (16 R) x (16 R): 256 threads, R x R outputs each. R = 4 for large outputs;
+// R = 2 or 1 when the 64 x 64 tiles would leave most SMs idle (e.g. the cfg1 layers at
+// batch 128), trading per-thread reuse for parallelism. Every output still accumulates its
+// k terms in ascending order.
 
 template <bool TA, bool TB>
 __device__ __forceinline__ float load_a(const float* A, int i, int k, int M, int K) {
@@ -32,32 +36,33 @@ __device__ __forceinline__ float load_b(const float* B, int k, int j, int K, int
 
 // MODE 0: out = act(bias_init + sum)     (plain c3.matmul)
 // MODE 1: s = sum + b[idx % bn]; out = maxnum(s, 0); z = s; mask bits (region forward)
-template <bool TA, bool TB, int MODE>
+template <bool TA, bool TB, int MODE, int R>
 __global__ void __launch_bounds__(256)
     sgemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B,
                        float* __restrict__ out, float* __restrict__ z, uint32_t* __restrict__ mask,
                        const float* __restrict__ bias, int64_t bias_numel, int M, int K, int N,
                        int act) {
+  constexpr int TM = 16 * R, TN = 16 * R;
   __shared__ float As[TK][TM + 4];
   __shared__ float Bs[TK][TN + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
-  float acc[4][4];
+  float acc[R][R];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < R; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < R; ++j) {
       float init = 0.f;
       if (MODE == 0 && bias != nullptr) {
-        const int col = n0 + tx * 4 + j;
+        const int col = n0 + tx * R + j;
         init = (col < N) ? bias[bias_numel == 1 ? 0 : col] : 0.f;
       }
       acc[i][j] = init;
     }
   for (int k0 = 0; k0 < K; k0 += TK) {
-    // 256 threads load 64x16 of A and 16x64 of B (4 elements each)
+    // 256 threads load TM x 16 of A and 16 x TN of B (R elements each)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < R; ++r) {
       const int e = threadIdx.x + r * 256;
       const int am = e / TK, ak = e % TK;  // A tile: [TM][TK]
       As[ak][am] = load_a<TA, TB>(A, m0 + am, k0 + ak, M, K);
@@ -67,25 +72,25 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     const int kmax = min(TK, K - k0);
     for (int kk = 0; kk < kmax; ++kk) {
-      float a[4], b[4];
+      float a[R], b[R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+      for (int i = 0; i < R; ++i) a[i] = As[kk][ty * R + i];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+      for (int j = 0; j < R; ++j) b[j] = Bs[kk][tx * R + j];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+        for (int j = 0; j < R; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int row = m0 + ty * 4 + i;
+  for (int i = 0; i < R; ++i) {
+    const int row = m0 + ty * R + i;
     if (row >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = n0 + tx * 4 + j;
+    for (int j = 0; j < R; ++j) {
+      const int col = n0 + tx * R + j;
       if (col >= N) continue;
       const int64_t idx = (int64_t)row * N + col;
       const float t = acc[i][j];
@@ -119,18 +124,30 @@ __global__ void __launch_bounds__(256)
   out[j] = s;
 }
 
-template <bool TA, bool TB, int MODE>
-int launch(const float* A, const float* B, float* out, float* z, uint32_t* mask, const float* bias,
-           int64_t bias_numel, int64_t M, int64_t K, int64_t N, int act, cudaStream_t st) {
-  dim3 grid(static_cast<unsigned>((N + TN - 1) / TN), static_cast<unsigned>((M + TM - 1) / TM));
+template <bool TA, bool TB, int MODE, int R>
+int launch_r(const float* A, const float* B, float* out, float* z, uint32_t* mask, const float* bias,
+             int64_t bias_numel, int64_t M, int64_t K, int64_t N, int act, cudaStream_t st) {
+  constexpr int T = 16 * R;
+  dim3 grid(static_cast<unsigned>((N + T - 1) / T), static_cast<unsigned>((M + T - 1) / T));
   if (grid.y > 65535) {
     set_error("exact matmul: M=%lld too large", (long long)M);
     return C3CU_ERR_INVALID;
   }
-  sgemm_exact_kernel<TA, TB, MODE><<<grid, 256, 0, st>>>(A, B, out, z, mask, bias, bias_numel,
-                                                         static_cast<int>(M), static_cast<int>(K),
-                                                         static_cast<int>(N), act);
+  sgemm_exact_kernel<TA, TB, MODE, R><<<grid, 256, 0, st>>>(A, B, out, z, mask, bias, bias_numel,
+                                                            static_cast<int>(M), static_cast<int>(K),
+                                                            static_cast<int>(N), act);
   return cuda_status(cudaGetLastError(), "exact matmul: launch");
+}
+
+// Largest register tile whose grid still gives every SM at least two blocks.
+template <bool TA, bool TB, int MODE>
+int launch(const float* A, const float* B, float* out, float* z, uint32_t* mask, const float* bias,
+           int64_t bias_numel, int64_t M, int64_t K, int64_t N, int act, cudaStream_t st) {
+  const int64_t want = 2 * static_cast<int64_t>(sm_count());
+  auto tiles = [&](int64_t t) { return ((M + t - 1) / t) * ((N + t - 1) / t); };
+  if (tiles(64) >= want) return launch_r<TA, TB, MODE, 4>(A, B, out, z, mask, bias, bias_numel, M, K, N, act, st);
+  if (tiles(32) >= want) return launch_r<TA, TB, MODE, 2>(A, B, out, z, mask, bias, bias_numel, M, K, N, act, st);
+  return launch_r<TA, TB, MODE, 1>(A, B, out, z, mask, bias, bias_numel, M, K, N, act, st);
 }
 
 template <int MODE>

@@ -3,7 +3,8 @@
     python -m c3_b200.profiling <case> [--iters N] [--m M] [--n N] [--k K] [--elems E]
                                 [--variant V] [--dw-dtype bf16|fp32]
 
-cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step, attn
+cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step, attn, mlp-step,
+       mlp-step-graph (the cfg1 training step, eager launches or one CUDA graph)
 Prints the CUDA-event time per launch and the algorithmic rate (TFLOP/s or GB/s)."""
 from __future__ import annotations
 
@@ -60,6 +61,20 @@ def _case(args, dev):
         L = torch.empty((B, H, S), device=dev)
         flops = 2.0 * B * H * S * S * 128  # causal: half of 4 B H S^2 D
         return (lambda: flash_attn_fwd(Q, K, V, True, None, O, L)), flops, "TFLOP/s"
+    if args.case in ("mlp-step", "mlp-step-graph"):
+        from . import mlp
+        params = mlp.init_params(1234, dev)
+        step = mlp.MLPTrainStep(params, batch=128, lr=0.01)
+        x, y = mlp.synthetic_batch(1, 128, dev)
+        d = mlp.LAYERS
+        fl = 2.0 * 128 * sum(a * b for a, b in zip(d[:-1], d[1:]))  # forward
+        fl += fl + 2.0 * 128 * (d[1] * d[2] + d[2] * d[3])  # dW of all layers + dX of layers 2, 3
+        if args.case == "mlp-step":
+            return (lambda: step.step(x, y)), fl, "TFLOP/s"
+        step.capture()
+        step.x_static.copy_(x)
+        step.y_static.copy_(y)
+        return (lambda: step.replay()), fl, "TFLOP/s"
     if args.case == "sum-rows":
         x = torch.randn((M, N), generator=g, device=dev)
         out = torch.empty(N, device=dev)

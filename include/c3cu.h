@@ -225,6 +225,21 @@ int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint32_t* local_
                         int64_t bf16_offset, int64_t bf16_count, int64_t f32_offset, int64_t f32_count,
                         int rank, int world, uint32_t epoch, int num_ctas, c3cu_stream_t stream);
 
+/* ------------------------------------------------------------------ training step (cfg1)
+ * Softmax cross-entropy over C classes, mean over B rows, fp32, one kernel:
+ *   lse_i = m_i + log(sum_c exp(z[i][c] - m_i)),  m_i = max_c z[i][c]  (c ascending)
+ *   *loss = (sum_i (lse_i - z[i][labels[i]])) / B   (i ascending for B <= 8192)
+ *   dlogits[i][c] = (exp(z[i][c] - lse_i) - (c == labels[i])) * (1 / B)   (may be NULL)
+ * A label outside [0, C) makes the loss and that row of dlogits NaN. The reference trains
+ * with its host framework's loss, which is not part of its sources: textbook definition. */
+int c3cu_softmax_ce_f32(const float* logits, const int32_t* labels, float* loss, float* dlogits,
+                        int64_t B, int64_t C, c3cu_stream_t stream);
+/* Plain SGD over `count` (1..C3CU_SGD_MAX_TENSORS) fp32 tensors in one launch:
+ * params[t][i] = params[t][i] - lr * grads[t][i] (multiply, then subtract; no FMA). */
+#define C3CU_SGD_MAX_TENSORS 8
+int c3cu_sgd_f32(float* const* params, const float* const* grads, const int64_t* numels, int count,
+                 float lr, c3cu_stream_t stream);
+
 /* Gradient all-reduce (sum, in place) through an NCCL communicator: `count` elements of
  * `dtype` (C3CU_DTYPE_F32 or C3CU_DTYPE_BF16) at `grads` on `stream`. `comm` is an
  * ncclComm_t, e.g. from c3cu_nccl_comm_init, whose id rank 0 made with c3cu_nccl_unique_id

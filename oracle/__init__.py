@@ -155,3 +155,53 @@ def attention_rows(q, k, v, scale, causal=True, rows=None):
     lib().c3o_attention_rows(_f(q), _f(k), _f(v), _f(o), _f(lse), S, D, scale, 1 if causal else 0,
                              r0, r1, _f(scratch))
     return o[r0:r1], lse[r0:r1]
+
+
+def softmax_ce(z, y):
+    """Mean softmax cross-entropy and its gradient w.r.t. the logits (textbook; see c3_oracle.c)."""
+    z = np.ascontiguousarray(z, dtype=np.float32)
+    y = np.ascontiguousarray(y, dtype=np.int32)
+    B, C = z.shape
+    loss = np.zeros(1, dtype=np.float32)
+    dz = np.empty_like(z)
+    lib().c3o_softmax_ce(_f(z), y.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _f(loss), _f(dz), B, C)
+    return float(loss[0]), dz
+
+
+def sgd(p, g, lr):
+    p = np.array(p, dtype=np.float32, copy=True)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    lib().c3o_sgd(_f(p), _f(g), p.size, ctypes.c_float(lr))
+    return p
+
+
+def mlp_train_step(params, x, y, lr):
+    """One cfg1 training step of the MLP 784 -> 256 -> 128 -> 10 (bias + ReLU on the hidden
+    layers, softmax cross-entropy, SGD) composed from the restated kernels, in the order the
+    reference's captured path evaluates it:
+      forward  z1 = x W1 + b1, a1 = relu(z1)   (MatMul+Add+ReLU region, W as [K, N])
+               z2 = a1 W2 + b2, a2 = relu(z2)
+               z3 = a2 W3 + b3                 (MatMul with the Add as bias epilogue)
+      loss, dz3 = softmax_ce(z3, y)
+      backward dW3 = a2^T dz3, db3 = sum_rows dz3, da2 = dz3 W3^T, dz2 = (z2 > 0) * da2, ...
+      update   p = p - lr * grad for W1, b1, W2, b2, W3, b3
+    params: dict of float32 arrays W1 [784, 256], b1 [256], W2 [256, 128], b2 [128],
+    W3 [128, 10], b3 [10]. Returns (loss, logits, grads dict, updated params dict)."""
+    W1, b1, W2, b2, W3, b3 = (params[k] for k in ("W1", "b1", "W2", "b2", "W3", "b3"))
+    a1, z1 = region_fwd(x, W1, b1)
+    a2, z2 = region_fwd(a1, W2, b2)
+    z3 = matmul(a2, W3, bias=b3)
+    loss, dz3 = softmax_ce(z3, y)
+    g = {}
+    g["W3"] = matmul(a2, dz3, transA=True)
+    g["b3"] = sum_reduce(dz3, 0)
+    da2 = matmul(dz3, W3, transB=True)
+    dz2 = relu_bwd(da2, z2)
+    g["W2"] = matmul(a1, dz2, transA=True)
+    g["b2"] = sum_reduce(dz2, 0)
+    da1 = matmul(dz2, W2, transB=True)
+    dz1 = relu_bwd(da1, z1)
+    g["W1"] = matmul(x, dz1, transA=True)
+    g["b1"] = sum_reduce(dz1, 0)
+    new = {k: sgd(params[k], g[k], lr) for k in params}
+    return loss, z3, g, new

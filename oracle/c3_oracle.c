@@ -296,3 +296,47 @@ C3O_EXPORT void c3o_attention_rows(const float* q, const float* k, const float* 
     if (lse) lse[i] = (float)((double)m + log(l));
   }
 }
+
+/* ------------------------------------------------------------------ training step (cfg1)
+ * The reference trains its MLP with the host framework's loss and optimizer, which are not
+ * part of the reference sources (CTorch): these are the textbook definitions, in the order
+ * the CUDA kernels use (parity unpinned).
+ * Softmax cross-entropy, mean over B rows:
+ *   m = max_c z[i][c]; s = sum_c expf(z[i][c] - m) (c ascending); lse = m + logf(s)
+ *   loss = (sum_i (lse_i - z[i][y_i])) / B   (i ascending; the product with 1/B)
+ *   dz[i][c] = (expf(z[i][c] - lse_i) - (c == y_i)) * (1 / B)
+ * A label outside [0, C) makes that row's loss (so the total) and its dz row NaN. */
+C3O_EXPORT void c3o_softmax_ce(const float* z, const int32_t* y, float* loss, float* dz, size_t B, size_t C) {
+  const float invB = 1.f / (float)B;
+  float total = 0.f;
+  for (size_t i = 0; i < B; ++i) {
+    const float* zr = z + i * C;
+    float* dr = dz ? dz + i * C : NULL;
+    const int32_t label = y[i];
+    float li;
+    if (label < 0 || (size_t)label >= C) {
+      li = NAN;
+      if (dr)
+        for (size_t c = 0; c < C; ++c) dr[c] = NAN;
+    } else {
+      float m = zr[0];
+      for (size_t c = 1; c < C; ++c) m = fmaxf(m, zr[c]);
+      float s = 0.f;
+      for (size_t c = 0; c < C; ++c) s = s + expf(zr[c] - m);
+      const float lse = m + logf(s);
+      li = lse - zr[label];
+      if (dr)
+        for (size_t c = 0; c < C; ++c) {
+          const float pc = expf(zr[c] - lse);
+          dr[c] = (pc - ((int32_t)c == label ? 1.f : 0.f)) * invB;
+        }
+    }
+    total = total + li;
+  }
+  *loss = total * invB;
+}
+
+/* SGD: p[i] = p[i] - lr * g[i] (multiply, then subtract). */
+C3O_EXPORT void c3o_sgd(float* p, const float* g, size_t n, float lr) {
+  for (size_t i = 0; i < n; ++i) p[i] = p[i] - lr * g[i];
+}
