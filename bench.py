@@ -207,8 +207,11 @@ def run_c3(args):
 
     import c3_b200
     from c3_b200.data_parallel import LinearReluTrainStep, default_overlap, env_grad_dtype, shard_rows
-    c3_b200.load()
+    L = c3_b200.load()
     c3_b200.device_check()
+    gemm_variant = int(os.environ.get("C3_GEMM_VARIANT", "0"))  # c3cu_set_gemm_variant
+    if gemm_variant:
+        c3_b200._lib.check(L.c3cu_set_gemm_variant(gemm_variant), "c3cu_set_gemm_variant")
 
     r_lo, r_hi = shard_rows(M_GLOBAL, world, rank)
     M = r_hi - r_lo
