@@ -64,6 +64,8 @@ _SIGNATURES = {
     "c3cu_nvls_allreduce_f32": ([_vp, _vp, _vp, _i64, _i64, _i, _i, ctypes.c_uint32, _i, _vp], _i),
     "c3cu_relu_mask_db_noalloc": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp], _i),
     "c3cu_set_attn_variant": ([_i], _i),
+    "c3cu_ew_program_multi": ([_vp, _vp, _i, _vp, _i, _vp, _i, _vp, _vp, _i, _i64, _vp], _i),
+    "c3cu_ew_backward_chain": ([_vp, _i, _vp, _vp, _vp, _i64, _vp], _i),
     "c3cu_softmax_ce_f32": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp], _i),
     "c3cu_sgd_f32": ([_vp, _vp, _vp, _i, ctypes.c_float, _vp], _i),
     "c3cu_flash_attn_fwd": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _i, _vp], _i),

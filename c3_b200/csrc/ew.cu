@@ -335,9 +335,11 @@ struct Program {
   int64_t numel[C3CU_EW_MAX_INPUTS];
   uint32_t code[C3CU_EW_MAX_INSTR];  // {op, dst, src0, src1} packed little-endian
   float consts[16];
+  float* out[C3CU_EW_MAX_OUTPUTS];
+  int out_reg[C3CU_EW_MAX_OUTPUTS];
   int n_inputs;
   int n_instr;
-  int out_reg;
+  int n_out;
 };
 
 __device__ __forceinline__ float ew_apply(uint32_t op, float a, float b, float cst) {
@@ -366,8 +368,7 @@ __device__ __forceinline__ float ew_apply(uint32_t op, float a, float b, float c
 
 // Registers live in a per-thread array; each thread evaluates the program on 4 adjacent
 // elements so that every decoded instruction is amortised over a 128-bit vector.
-__global__ void __launch_bounds__(256) program_kernel(const Program prog, float* __restrict__ out,
-                                                      int64_t n) {
+__global__ void __launch_bounds__(256) program_kernel(const Program prog, int64_t n) {
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = tid * 4; base < n; base += nthreads * 4) {
@@ -394,13 +395,16 @@ __global__ void __launch_bounds__(256) program_kernel(const Program prog, float*
 #pragma unroll
       for (int e = 0; e < 4; ++e) reg[dst][e] = ew_apply(op, reg[s0][e], reg[s1][e], cst);
     }
-    const int o = prog.out_reg;
-    if (full && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0u)) {
-      __stcs(reinterpret_cast<float4*>(out + base), make_float4(reg[o][0], reg[o][1], reg[o][2], reg[o][3]));
-    } else {
+    for (int j = 0; j < prog.n_out; ++j) {
+      const int o = prog.out_reg[j];
+      float* out = prog.out[j];
+      if (full && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0u)) {
+        __stcs(reinterpret_cast<float4*>(out + base), make_float4(reg[o][0], reg[o][1], reg[o][2], reg[o][3]));
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (base + e < n) out[base + e] = reg[o][e];
+        for (int e = 0; e < 4; ++e)
+          if (base + e < n) out[base + e] = reg[o][e];
+      }
     }
   }
 }
@@ -565,27 +569,36 @@ int c3cu_convert(const void* in, int in_dtype, void* out, int out_dtype, int64_t
   return c3cu::cuda_status(cudaGetLastError(), "convert: launch");
 }
 
-int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,
-                    const uint8_t* code, int n_instr, const float* constants, int n_constants,
-                    int out_reg, float* out, int64_t n, c3cu_stream_t stream) {
+int c3cu_ew_program_multi(const float* const* inputs, const int64_t* numels, int n_inputs,
+                          const uint8_t* code, int n_instr, const float* constants, int n_constants,
+                          const int* out_regs, float* const* outs, int n_out, int64_t n,
+                          c3cu_stream_t stream) {
   int rc = c3cu::require_sm100();
   if (rc != C3CU_OK) return rc;
   if (n < 0 || n_inputs < 0 || n_inputs > C3CU_EW_MAX_INPUTS || n_instr < 0 ||
-      n_instr > C3CU_EW_MAX_INSTR || n_constants < 0 || n_constants > 16 || out_reg < 0 ||
-      out_reg > 15) {
-    c3cu::set_error("ew_program: bad program shape (inputs %d, instructions %d, constants %d)",
-                    n_inputs, n_instr, n_constants);
+      n_instr > C3CU_EW_MAX_INSTR || n_constants < 0 || n_constants > 16 || n_out < 1 ||
+      n_out > C3CU_EW_MAX_OUTPUTS || !out_regs || !outs) {
+    c3cu::set_error("ew_program: bad program shape (inputs %d, instructions %d, constants %d, outputs %d)",
+                    n_inputs, n_instr, n_constants, n_out);
     return C3CU_ERR_INVALID;
   }
   if (n == 0) return C3CU_OK;
-  if (!out || (n_inputs > 0 && (!inputs || !numels)) || (n_instr > 0 && !code)) {
+  if ((n_inputs > 0 && (!inputs || !numels)) || (n_instr > 0 && !code)) {
     c3cu::set_error("ew_program: null pointer");
     return C3CU_ERR_INVALID;
   }
   c3cu::ew::Program prog{};
   prog.n_inputs = n_inputs;
   prog.n_instr = n_instr;
-  prog.out_reg = out_reg;
+  prog.n_out = n_out;
+  for (int j = 0; j < n_out; ++j) {
+    if (out_regs[j] < 0 || out_regs[j] > 15 || !outs[j]) {
+      c3cu::set_error("ew_program: output %d: bad register %d or null pointer", j, out_regs[j]);
+      return C3CU_ERR_INVALID;
+    }
+    prog.out_reg[j] = out_regs[j];
+    prog.out[j] = outs[j];
+  }
   for (int i = 0; i < n_inputs; ++i) {
     if (!inputs[i] || numels[i] <= 0) {
       c3cu::set_error("ew_program: input %d is null or empty", i);
@@ -611,8 +624,110 @@ int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inp
   }
   for (int c = 0; c < n_constants; ++c) prog.consts[c] = constants[c];
   const int grid = c3cu::ew::grid_for((n + 3) / 4, 256);
-  c3cu::ew::program_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(prog, out, n);
+  c3cu::ew::program_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(prog, n);
   return c3cu::cuda_status(cudaGetLastError(), "ew_program: launch");
+}
+
+int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inputs,
+                    const uint8_t* code, int n_instr, const float* constants, int n_constants,
+                    int out_reg, float* out, int64_t n, c3cu_stream_t stream) {
+  float* outs[1] = {out};
+  return c3cu_ew_program_multi(inputs, numels, n_inputs, code, n_instr, constants, n_constants, &out_reg,
+                               outs, 1, n, stream);
+}
+
+// Fused backward of a chain of unary elementwise nodes in one pass. Each node's gradient is
+// the graph the reference builds for it (src/C3/C3BackwardCapture.cpp:501-617, 725-743,
+// 823-872), one IEEE operation per graph node (the fused backward graphs are compiled without
+// secondary fusion, :1236-1246, so Div is a plain division):
+//   ReLU     Mul(Gt(x, 0), g)
+//   Sigmoid  s = Div(1, Add(1, Exp(Neg(x)))); Mul(g, Mul(s, Sub(1, s)))
+//   Tanh     t = Div(Sub(Exp(x), Exp(Neg(x))), Add(Exp(x), Exp(Neg(x)))); Mul(g, Sub(1, Mul(t, t)))
+//   Neg      Neg(g)
+//   Exp      Mul(Exp(x), g)
+//   Log      Div(g, x)
+// Registers: 0 = incoming gradient, 1..N = the nodes' forward inputs, then each node's
+// output gradient, then temporaries (constant table: 0 -> 0.0, 1 -> 1.0).
+int c3cu_ew_backward_chain(const int* node_ops, int n_nodes, const float* grad, const float* const* xs,
+                           float* const* outs, int64_t n, c3cu_stream_t stream) {
+  if (!node_ops || n_nodes < 1 || n_nodes > C3CU_BW_MAX_CHAIN || !grad || !outs) {
+    c3cu::set_error("ew_backward_chain: 1 to %d nodes expected, got %d", C3CU_BW_MAX_CHAIN, n_nodes);
+    return C3CU_ERR_INVALID;
+  }
+  std::vector<uint8_t> code;
+  auto emit = [&](int op, int dst, int s0, int s1) {
+    code.push_back(static_cast<uint8_t>(op));
+    code.push_back(static_cast<uint8_t>(dst));
+    code.push_back(static_cast<uint8_t>(s0));
+    code.push_back(static_cast<uint8_t>(s1));
+  };
+  const float* inputs[C3CU_EW_MAX_INPUTS] = {grad};
+  int64_t numels[C3CU_EW_MAX_INPUTS] = {n};
+  int n_inputs = 1 + n_nodes;
+  for (int k = 0; k < n_nodes; ++k) {
+    const int op = node_ops[k];
+    if (op < C3CU_BW_RELU || op > C3CU_BW_LOG) {
+      c3cu::set_error("ew_backward_chain: node %d has unknown type %d", k, op);
+      return C3CU_ERR_INVALID;
+    }
+    const float* x = xs ? xs[k] : nullptr;
+    if (op != C3CU_BW_NEG && !x) {
+      c3cu::set_error("ew_backward_chain: node %d needs its forward input", k);
+      return C3CU_ERR_INVALID;
+    }
+    inputs[1 + k] = x ? x : grad;  // Neg reads no forward input; any valid pointer will do
+    numels[1 + k] = n;
+  }
+  const int t0 = 1 + 2 * n_nodes, t1 = t0 + 1, t2 = t0 + 2;  // temporaries (<= 11, 12, 13)
+  int g = 0;
+  int out_regs[C3CU_EW_MAX_OUTPUTS];
+  for (int k = 0; k < n_nodes; ++k) {
+    const int x = 1 + k, o = 1 + n_nodes + k;
+    switch (node_ops[k]) {
+      case C3CU_BW_RELU:
+        emit(C3CU_EW_CONST, t0, 0, 0);
+        emit(C3CU_EW_GT, t0, x, t0);
+        emit(C3CU_EW_MUL, o, t0, g);
+        break;
+      case C3CU_BW_SIGMOID:
+        emit(C3CU_EW_NEG, t0, x, 0);
+        emit(C3CU_EW_EXP, t0, t0, 0);
+        emit(C3CU_EW_CONST, t1, 1, 0);
+        emit(C3CU_EW_ADD, t0, t1, t0);
+        emit(C3CU_EW_DIV, t0, t1, t0);  // s
+        emit(C3CU_EW_SUB, t2, t1, t0);
+        emit(C3CU_EW_MUL, t0, t0, t2);
+        emit(C3CU_EW_MUL, o, g, t0);
+        break;
+      case C3CU_BW_TANH:
+        emit(C3CU_EW_EXP, t0, x, 0);
+        emit(C3CU_EW_NEG, t1, x, 0);
+        emit(C3CU_EW_EXP, t1, t1, 0);
+        emit(C3CU_EW_SUB, t2, t0, t1);
+        emit(C3CU_EW_ADD, t0, t0, t1);
+        emit(C3CU_EW_DIV, t0, t2, t0);  // t
+        emit(C3CU_EW_MUL, t0, t0, t0);
+        emit(C3CU_EW_CONST, t1, 1, 0);
+        emit(C3CU_EW_SUB, t0, t1, t0);
+        emit(C3CU_EW_MUL, o, g, t0);
+        break;
+      case C3CU_BW_NEG:
+        emit(C3CU_EW_NEG, o, g, 0);
+        break;
+      case C3CU_BW_EXP:
+        emit(C3CU_EW_EXP, t0, x, 0);
+        emit(C3CU_EW_MUL, o, t0, g);
+        break;
+      case C3CU_BW_LOG:
+        emit(C3CU_EW_DIV, o, g, x);
+        break;
+    }
+    out_regs[k] = o;
+    g = o;
+  }
+  const float consts[2] = {0.f, 1.f};
+  return c3cu_ew_program_multi(inputs, numels, n_inputs, code.data(), static_cast<int>(code.size() / 4), consts,
+                               2, out_regs, outs, n_nodes, n, stream);
 }
 
 }  // extern "C"

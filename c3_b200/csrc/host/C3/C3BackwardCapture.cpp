@@ -1,7 +1,11 @@
 #include "C3/C3BackwardCapture.h"
 
+#include <algorithm>
 #include <sstream>
 #include <typeinfo>
+
+#include "C3/CudaKernels.h"
+#include "c3cu.h"
 
 #include "C3/C3Config.h"
 #include "CtorchError.h"
@@ -180,6 +184,9 @@ C3BackwardCapture::Stats C3BackwardCapture::getStats() const {
   s.cache_hit_count = cache_hit_count_;
   s.cache_miss_count = cache_miss_count_;
   s.execution_failures = execution_failures_;
+  s.fusion_compile_count = fusion_compile_count_;
+  s.fusion_hit_count = fusion_hit_count_;
+  s.fusion_miss_count = fusion_miss_count_;
   return s;
 }
 
@@ -187,13 +194,264 @@ void C3BackwardCapture::clear() {
   {
     std::lock_guard<std::mutex> lock(stats_mutex_);
     capture_count_ = compile_count_ = cache_hit_count_ = cache_miss_count_ = execution_failures_ = 0;
+    fusion_compile_count_ = fusion_hit_count_ = fusion_miss_count_ = 0;
   }
   waitForPendingCompiles();
+  {
+    std::lock_guard<std::mutex> lock(fusion_mutex_);
+    recent_sequence_.clear();
+    recent_grad_shapes_.clear();
+    recent_input_shapes_.clear();
+    sequence_counts_.clear();
+  }
+  clearInterceptedState();
   std::lock_guard<std::mutex> lock(pending_mutex_);
   pending_compiles_.clear();
 }
 
-void C3BackwardCapture::clearCallScopedState() {}
+void C3BackwardCapture::clearCallScopedState() { clearInterceptedState(); }
+
+// ============================================================================ fused sequences
+bool C3BackwardCapture::isElementWiseBackward(const std::string& t) {
+  // single-input, single-output nodes only (src/C3/C3BackwardCapture.cpp:463-483)
+  for (const char* n : {"ReLUNode", "SigmoidNode", "TanhNode", "NegNode", "GELUNode", "LReLUNode", "SinNode",
+                        "CosNode", "AbsNode", "ExpNode", "LogNode", "MinNode", "MaxNode"})
+    if (t.find(n) != std::string::npos) return true;
+  return false;
+}
+
+bool C3BackwardCapture::isFusableSequence(const std::vector<std::string>& types) {
+  if (types.size() < 2) return false;
+  for (const auto& t : types)
+    if (!isElementWiseBackward(t)) return false;
+  return true;
+}
+
+std::string C3BackwardCapture::makeSequenceKey(const std::vector<std::string>& types) {
+  std::string key;
+  for (const auto& t : types) {
+    if (!key.empty()) key += "+";
+    const char* names[][2] = {{"ReLUNode", "ReLU"}, {"SigmoidNode", "Sigmoid"}, {"TanhNode", "Tanh"},
+                              {"NegNode", "Neg"},   {"AddNode", "Add"},         {"SubNode", "Sub"},
+                              {"MulNode", "Mul"},   {"DivNode", "Div"},         {"ExpNode", "Exp"},
+                              {"LogNode", "Log"}};
+    const char* shortname = "Other";
+    for (const auto& nm : names)
+      if (t.find(nm[0]) != std::string::npos) {
+        shortname = nm[1];
+        break;
+      }
+    key += shortname;
+  }
+  return key;
+}
+
+std::string C3BackwardCapture::makeFusedBackwardKey(const std::string& seq_key, const std::vector<size_t>& g,
+                                                    const std::vector<size_t>& in) {
+  std::stringstream ss;
+  ss << "backward_fused_" << seq_key << "|g:";
+  for (size_t v : g) ss << v << ",";
+  ss << "|i:";
+  for (size_t v : in) ss << v << ",";
+  return ss.str();
+}
+
+void C3BackwardCapture::countSequence(std::vector<std::string> types, std::vector<std::vector<size_t>> gs,
+                                      std::vector<std::vector<size_t>> is) {
+  // registration key: the most downstream gradient shape and the most upstream input shape
+  const std::string full_key = makeFusedBackwardKey(makeSequenceKey(types), gs.front(), is.back());
+  auto& entry = sequence_counts_[full_key];
+  if (entry.node_types.empty()) {
+    entry.node_types = std::move(types);
+    entry.grad_shapes = std::move(gs);
+    entry.input_shapes = std::move(is);
+  }
+  entry.frequency++;
+  if (entry.frequency >= kFusionThreshold && !entry.compiling) {
+    entry.compiling = true;
+    compileFusedBackwardAsync(entry);
+  }
+}
+
+void C3BackwardCapture::recordBackwardNode(const std::string& node_type, const std::vector<size_t>& grad_shape,
+                                           const std::vector<size_t>& input_shape,
+                                           const std::vector<Tensor>& forward_inputs) {
+  (void)forward_inputs;
+  if (!isElementWiseBackward(node_type)) return;  // other nodes never enter the window
+  std::lock_guard<std::mutex> lock(fusion_mutex_);
+  // A complete two-node chain from the previous pass is counted and the window restarted,
+  // so that the tail of one iteration never pairs with the head of the next
+  // (src/C3/C3BackwardCapture.cpp:886-931).
+  if (recent_sequence_.size() == 2) {
+    std::vector<std::string> chain(recent_sequence_.begin(), recent_sequence_.end());
+    std::vector<std::vector<size_t>> gs(recent_grad_shapes_.begin(), recent_grad_shapes_.end());
+    std::vector<std::vector<size_t>> is(recent_input_shapes_.begin(), recent_input_shapes_.end());
+    bool same_shape = true;
+    for (size_t i = 1; i < gs.size(); ++i) same_shape = same_shape && gs[i] == gs[0];
+    if (same_shape && isFusableSequence(chain)) countSequence(std::move(chain), std::move(gs), std::move(is));
+    recent_sequence_.clear();
+    recent_grad_shapes_.clear();
+    recent_input_shapes_.clear();
+  }
+  recent_sequence_.push_back(node_type);
+  recent_grad_shapes_.push_back(grad_shape);
+  recent_input_shapes_.push_back(input_shape);
+  if (recent_sequence_.size() > kFusionWindowSize) {
+    recent_sequence_.pop_front();
+    recent_grad_shapes_.pop_front();
+    recent_input_shapes_.pop_front();
+  }
+  // every fusable tail window of length 2..kFusionWindowSize is counted
+  const size_t L = recent_sequence_.size();
+  for (size_t w = 2; w <= kFusionWindowSize && w <= L; ++w) {
+    const size_t start = L - w;
+    std::vector<std::string> types(recent_sequence_.begin() + start, recent_sequence_.end());
+    if (!isFusableSequence(types)) continue;
+    std::vector<std::vector<size_t>> gs(recent_grad_shapes_.begin() + start, recent_grad_shapes_.end());
+    std::vector<std::vector<size_t>> is(recent_input_shapes_.begin() + start, recent_input_shapes_.end());
+    countSequence(std::move(types), std::move(gs), std::move(is));
+  }
+}
+
+namespace {
+int chainOp(const std::string& t) {
+  if (t.find("ReLUNode") != std::string::npos) return C3CU_BW_RELU;
+  if (t.find("SigmoidNode") != std::string::npos) return C3CU_BW_SIGMOID;
+  if (t.find("TanhNode") != std::string::npos) return C3CU_BW_TANH;
+  if (t.find("NegNode") != std::string::npos) return C3CU_BW_NEG;
+  if (t.find("ExpNode") != std::string::npos) return C3CU_BW_EXP;
+  if (t.find("LogNode") != std::string::npos) return C3CU_BW_LOG;
+  return 0;  // no backward graph for this type: the sequence is not compiled
+}
+}  // namespace
+
+void C3BackwardCapture::compileFusedBackwardAsync(const BackwardSequence& seq) {
+  if (!isFusableSequence(seq.node_types) || seq.grad_shapes.empty() || seq.input_shapes.empty()) return;
+  const std::string key =
+      makeFusedBackwardKey(makeSequenceKey(seq.node_types), seq.grad_shapes.front(), seq.input_shapes.back());
+  {
+    std::lock_guard<std::mutex> lock(pending_mutex_);
+    if (pending_compiles_.count(key)) return;
+    pending_compiles_[key] = true;
+  }
+  auto task = [this, seq, key]() {
+    std::vector<int> ops;
+    for (const auto& t : seq.node_types) ops.push_back(chainOp(t));
+    const bool supported = std::find(ops.begin(), ops.end(), 0) == ops.end();
+    if (supported) {
+      // inputs [grad, fwd_0[0], ..., fwd_{N-1}[0]]: identity map onto the forward inputs
+      auto kernel = std::make_shared<CudaFusedBackwardKernel>(key, ops, seq.grad_shapes.front());
+      std::vector<size_t> fwd_map(seq.node_types.size());
+      for (size_t i = 0; i < fwd_map.size(); ++i) fwd_map[i] = i;
+      C3KernelRegistry::getInstance().installBackward(key, kernel, seq.grad_shapes.front(), seq.input_shapes.back(),
+                                                      fwd_map, 1 + seq.node_types.size());
+      std::lock_guard<std::mutex> lock(stats_mutex_);
+      fusion_compile_count_++;
+    }
+    std::lock_guard<std::mutex> lock(pending_mutex_);
+    pending_compiles_.erase(key);
+  };
+  std::lock_guard<std::mutex> lock(pending_mutex_);
+  futures_.push_back(std::async(std::launch::async, task));
+}
+
+std::optional<Tensor> C3BackwardCapture::tryExecuteFusedBackward(const ::Node* node, const Tensor& grad,
+                                                                 const std::vector<Tensor>& forward_inputs) {
+  if (!node) return std::nullopt;
+  const std::string current_type = typeid(*node).name();
+  // Path A: the gradient was computed when the fused kernel ran at a downstream node.
+  {
+    std::unique_lock<std::shared_mutex> lock(intercepted_mutex_);
+    auto it = pending_intercepted_.find(node);
+    if (it != pending_intercepted_.end()) {
+      if (it->second.first == current_type) {
+        Tensor t = std::move(it->second.second);
+        pending_intercepted_.erase(it);
+        lock.unlock();
+        std::lock_guard<std::mutex> slock(stats_mutex_);
+        fusion_hit_count_++;
+        return t;
+      }
+      pending_intercepted_.erase(it);  // a reused address with another type: stale entry
+    }
+  }
+  {
+    std::lock_guard<std::mutex> mlock(miss_marker_mutex_);
+    if (miss_marker_nodes_.count(node)) {
+      std::lock_guard<std::mutex> slock(stats_mutex_);
+      fusion_miss_count_++;
+      return std::nullopt;
+    }
+  }
+  if (!isElementWiseBackward(current_type)) return std::nullopt;
+  // Path B: this node is the most downstream one of a chain. Walk upstream (skipping up to
+  // kSkipMax single-upstream wrapper nodes between elementwise nodes); every node of the
+  // chain must take an input of the gradient's shape.
+  constexpr size_t kSkipMax = 4;
+  std::vector<std::shared_ptr<::Node>> chain_nodes{nullptr};
+  std::vector<std::string> chain_types{current_type};
+  std::vector<std::vector<Tensor>> chain_inputs{forward_inputs.empty() ? node->getInputs() : forward_inputs};
+  const ::Node* cur = node;
+  for (size_t step = 1; step < kFusionWindowSize; ++step) {
+    std::shared_ptr<::Node> next;
+    const ::Node* c = cur;
+    for (size_t skips = 0; skips <= kSkipMax; ++skips) {
+      const auto& ups = c->getUpStreamNodes();
+      if (ups.size() != 1 || !ups[0]) break;
+      if (isElementWiseBackward(typeid(*ups[0]).name())) {
+        next = ups[0];
+        break;
+      }
+      c = ups[0].get();
+    }
+    if (!next) break;
+    const auto& ins = next->getInputs();
+    if (ins.empty() || ins[0].sizes() != grad.sizes()) break;
+    chain_nodes.push_back(next);
+    chain_types.push_back(typeid(*next).name());
+    chain_inputs.push_back(ins);
+    cur = next.get();
+  }
+  for (size_t w = std::min(kFusionWindowSize, chain_types.size()); w >= 2; --w) {
+    std::vector<std::string> types(chain_types.begin(), chain_types.begin() + w);
+    if (!isFusableSequence(types)) continue;
+    const auto& up_shape = chain_inputs[w - 1].empty() ? grad.sizes() : chain_inputs[w - 1][0].sizes();
+    const std::string key = makeFusedBackwardKey(makeSequenceKey(types), grad.sizes(), up_shape);
+    if (!C3KernelRegistry::getInstance().hasBackwardKey(key)) continue;
+    std::vector<Tensor> fwd;
+    for (size_t k = 0; k < w; ++k) {
+      if (chain_inputs[k].empty()) break;
+      fwd.push_back(chain_inputs[k][0]);
+    }
+    if (fwd.size() != w) continue;
+    auto outs = C3KernelRegistry::getInstance().tryExecuteBackward(key, grad, fwd);
+    if (!outs || outs->size() != w) continue;
+    {
+      std::unique_lock<std::shared_mutex> lock(intercepted_mutex_);
+      for (size_t k = 1; k < w; ++k)
+        pending_intercepted_[chain_nodes[k].get()] = {chain_types[k], std::move((*outs)[k])};
+    }
+    std::lock_guard<std::mutex> slock(stats_mutex_);
+    fusion_hit_count_++;
+    return std::move((*outs)[0]);
+  }
+  {
+    std::lock_guard<std::mutex> mlock(miss_marker_mutex_);
+    miss_marker_nodes_[node] = true;
+  }
+  std::lock_guard<std::mutex> slock(stats_mutex_);
+  fusion_miss_count_++;
+  return std::nullopt;
+}
+
+void C3BackwardCapture::clearInterceptedState() {
+  {
+    std::unique_lock<std::shared_mutex> lock(intercepted_mutex_);
+    pending_intercepted_.clear();
+  }
+  std::lock_guard<std::mutex> lock(miss_marker_mutex_);
+  miss_marker_nodes_.clear();
+}
 
 bool C3BackwardCapture::needsSumReduce(const std::vector<size_t>& g, const std::vector<size_t>& t) {
   if (g == t) return false;

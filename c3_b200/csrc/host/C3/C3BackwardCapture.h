@@ -9,9 +9,11 @@
 // elementwise types), then bound to B200 kernels by C3Engine.
 #pragma once
 
+#include <deque>
 #include <future>
 #include <mutex>
 #include <optional>
+#include <shared_mutex>
 #include <string>
 #include <unordered_map>
 #include <utility>
@@ -70,6 +72,27 @@ class C3BackwardCapture {
   // Waits for every background compile (bounded per compile by 30 s).
   void waitForPendingCompiles();
 
+  // ---- fused backward sequences (src/C3/C3BackwardCapture.cpp:874-1637) ----------------
+  // The host records every backward node it visits; chains of 2..kFusionWindowSize unary
+  // elementwise nodes with one gradient shape are compiled (after kFusionThreshold sightings)
+  // into one multi-output kernel, installed under makeFusedBackwardKey. At the chain's most
+  // downstream node, tryExecuteFusedBackward walks upstream, runs the kernel once, returns
+  // that node's gradient and keeps the others; the upstream nodes then receive theirs from
+  // the intercept table (path A) without running anything.
+  static constexpr size_t kFusionWindowSize = 4;
+  static constexpr int kFusionThreshold = 1;
+  void recordBackwardNode(const std::string& node_type, const std::vector<size_t>& grad_shape,
+                          const std::vector<size_t>& input_shape, const std::vector<Tensor>& forward_inputs);
+  std::optional<Tensor> tryExecuteFusedBackward(const ::Node* node, const Tensor& grad,
+                                                const std::vector<Tensor>& forward_inputs);
+  static bool isElementWiseBackward(const std::string& node_type);
+  static bool isFusableSequence(const std::vector<std::string>& types);
+  static std::string makeSequenceKey(const std::vector<std::string>& types);
+  static std::string makeFusedBackwardKey(const std::string& seq_key, const std::vector<size_t>& grad_shape,
+                                          const std::vector<size_t>& input_shape);
+  // Drops intercepted gradients and miss markers (end of a backward pass).
+  void clearInterceptedState();
+
   static bool needsSumReduce(const std::vector<size_t>& grad_shape, const std::vector<size_t>& target_shape);
   static int computeReduceAxis(const std::vector<size_t>& grad_shape, const std::vector<size_t>& target_shape);
 
@@ -92,6 +115,26 @@ class C3BackwardCapture {
                                              const TensorDesc& b, size_t index);
   static BackwardGraph buildExpBackwardGraph(const TensorDesc& grad, const TensorDesc& x);
   static BackwardGraph buildLogBackwardGraph(const TensorDesc& grad, const TensorDesc& x);
+
+  struct BackwardSequence {
+    std::vector<std::string> node_types;
+    std::vector<std::vector<size_t>> grad_shapes, input_shapes;
+    int frequency = 0;
+    bool compiling = false;
+  };
+  void countSequence(std::vector<std::string> types, std::vector<std::vector<size_t>> gs,
+                     std::vector<std::vector<size_t>> is);
+  void compileFusedBackwardAsync(const BackwardSequence& seq);
+
+  std::mutex fusion_mutex_;
+  std::deque<std::string> recent_sequence_;
+  std::deque<std::vector<size_t>> recent_grad_shapes_, recent_input_shapes_;
+  std::unordered_map<std::string, BackwardSequence> sequence_counts_;
+  std::shared_mutex intercepted_mutex_;
+  std::unordered_map<const ::Node*, std::pair<std::string, Tensor>> pending_intercepted_;
+  std::mutex miss_marker_mutex_;
+  std::unordered_map<const ::Node*, bool> miss_marker_nodes_;
+  size_t fusion_compile_count_ = 0, fusion_hit_count_ = 0, fusion_miss_count_ = 0;
 
   mutable std::mutex stats_mutex_;
   size_t capture_count_ = 0, compile_count_ = 0, cache_hit_count_ = 0, cache_miss_count_ = 0;

@@ -246,6 +246,36 @@ std::vector<Tensor> CudaElementwiseKernel::run(const std::vector<Tensor>& in) {
   return {all_bf16 && !in.empty() ? convert(out, DType::kBF16) : out};
 }
 
+// ---------------------------------------------------------------------------- fused backward
+std::string CudaFusedBackwardKernel::describe() const {
+  return "fused backward chain of " + std::to_string(ops_.size()) + " unary nodes";
+}
+
+std::vector<Tensor> CudaFusedBackwardKernel::run(const std::vector<Tensor>& in) {
+  const size_t n = in[0].numel();
+  std::vector<Tensor> f32;  // fp32 copies keep the chain in fp32 whatever the input dtype
+  f32.reserve(in.size());
+  for (const auto& t : in) {
+    if (t.numel() != n) throw std::runtime_error(describe() + ": every input must have the gradient's size");
+    f32.push_back(convert(t, DType::kFloat));
+  }
+  std::vector<const float*> xs;
+  for (size_t k = 1; k < f32.size(); ++k) xs.push_back(static_cast<const float*>(f32[k].data()));
+  std::vector<Tensor> outs;
+  std::vector<float*> op;
+  for (size_t k = 0; k < ops_.size(); ++k) {
+    outs.push_back(newDevice(in[0].shape(), DType::kFloat));
+    op.push_back(static_cast<float*>(outs.back().data()));
+  }
+  checkAbi(c3cu_ew_backward_chain(ops_.data(), static_cast<int>(ops_.size()),
+                                  static_cast<const float*>(f32[0].data()), xs.data(), op.data(),
+                                  static_cast<int64_t>(n), stream()),
+           describe().c_str());
+  if (in[0].dtype() == DType::kBF16)
+    for (auto& o : outs) o = convert(o, DType::kBF16);
+  return outs;
+}
+
 // ---------------------------------------------------------------------------- lowering
 namespace {
 

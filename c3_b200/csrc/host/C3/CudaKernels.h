@@ -142,6 +142,24 @@ class CudaElementwiseKernel : public CudaKernelBase {
   size_t n_inputs_;
 };
 
+// Fused backward of a chain of unary elementwise nodes (the reference's fused backward
+// sequences): inputs [grad, x_0, ..., x_{N-1}] (x_k = node k's forward input, k = 0 most
+// downstream), outputs the N gradients the nodes pass upstream, from one pass
+// (c3cu_ew_backward_chain). node_ops are C3CU_BW_* codes.
+class CudaFusedBackwardKernel : public CudaKernelBase {
+ public:
+  CudaFusedBackwardKernel(std::string key, std::vector<int> node_ops, std::vector<size_t> shape)
+      : CudaKernelBase(std::move(key), Precision::kExactF32, std::move(shape)), ops_(std::move(node_ops)) {}
+  std::string describe() const override;
+  size_t expectedInputs() const override { return 1 + ops_.size(); }
+
+ protected:
+  std::vector<Tensor> run(const std::vector<Tensor>& in) override;
+
+ private:
+  std::vector<int> ops_;
+};
+
 // Lowers a graph (after dead-code elimination) onto one of the kernels above; throws
 // std::runtime_error when the graph is outside what the B200 kernels implement.
 std::shared_ptr<CudaKernelBase> lowerGraph(const Graph& graph, const CompileOptions& options,

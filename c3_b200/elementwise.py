@@ -57,3 +57,23 @@ def sum_rows(x: torch.Tensor, out: torch.Tensor | None = None):
     rc = L.c3cu_sum_rows_f32(_p(x), _p(out), M, N, _p(ws), ws.numel(), _stream(x.device))
     _lib.check(rc, "c3cu_sum_rows_f32")
     return out
+
+
+BW_OPS = {"ReLU": 1, "Sigmoid": 2, "Tanh": 3, "Neg": 4, "Exp": 5, "Log": 6}
+
+
+def backward_chain(types: list[str], grad: torch.Tensor, xs: list[torch.Tensor | None],
+                   outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
+    """Fused backward of a chain of unary elementwise nodes (types[0] most downstream):
+    returns the gradient each node passes upstream, from one pass (c3cu_ew_backward_chain)."""
+    n = grad.numel()
+    if outs is None:
+        outs = [torch.empty_like(grad) for _ in types]
+    ops = (ctypes.c_int * len(types))(*[BW_OPS[t] for t in types])
+    xp = (ctypes.c_void_p * len(types))(*[0 if x is None else x.data_ptr() for x in xs])
+    op = (ctypes.c_void_p * len(types))(*[o.data_ptr() for o in outs])
+    rc = _lib.load().c3cu_ew_backward_chain(ctypes.cast(ops, ctypes.c_void_p), len(types), _p(grad),
+                                            ctypes.cast(xp, ctypes.c_void_p), ctypes.cast(op, ctypes.c_void_p),
+                                            n, _stream(grad.device))
+    _lib.check(rc, "c3cu_ew_backward_chain")
+    return outs

@@ -165,7 +165,8 @@ int c3cu_ew_chain_cfg4(const float* A, const float* B, const float* C, float* ou
  * from inputs[i][idx % numels[i]] (numels[i] == n: no broadcast), and register `out_reg`
  * is stored to out[idx]. Opcodes: see C3CU_EW_* below. */
 #define C3CU_EW_MAX_INPUTS 8
-#define C3CU_EW_MAX_INSTR 32
+#define C3CU_EW_MAX_INSTR 64
+#define C3CU_EW_MAX_OUTPUTS 4
 #define C3CU_EW_ADD 1
 #define C3CU_EW_SUB 2
 #define C3CU_EW_MUL 3
@@ -186,6 +187,28 @@ int c3cu_ew_program(const float* const* inputs, const int64_t* numels, int n_inp
                     int out_reg, float* out, int64_t n, c3cu_stream_t stream);
 
 /* out[i] = in[i] converted between C3CU_DTYPE_F32 and C3CU_DTYPE_BF16 (round to nearest even). */
+/* The same register machine with up to C3CU_EW_MAX_OUTPUTS outputs: outs[j] receives
+ * register out_regs[j], all from one pass over the inputs. */
+int c3cu_ew_program_multi(const float* const* inputs, const int64_t* numels, int n_inputs,
+                          const uint8_t* code, int n_instr, const float* constants, int n_constants,
+                          const int* out_regs, float* const* outs, int n_out, int64_t n,
+                          c3cu_stream_t stream);
+
+/* Fused backward of a chain of unary elementwise nodes (the reference's fused backward
+ * sequences, src/C3/C3BackwardCapture.cpp:874-1637), one pass over n fp32 elements.
+ * node_ops[k] (k = 0 is the most downstream node, the first in backward order) is one of
+ * C3CU_BW_*; xs[k] is that node's forward input (unused for Neg); outs[k] receives the
+ * gradient node k passes upstream, i.e. the input gradient of node k + 1. */
+#define C3CU_BW_RELU 1
+#define C3CU_BW_SIGMOID 2
+#define C3CU_BW_TANH 3
+#define C3CU_BW_NEG 4
+#define C3CU_BW_EXP 5
+#define C3CU_BW_LOG 6
+#define C3CU_BW_MAX_CHAIN 4
+int c3cu_ew_backward_chain(const int* node_ops, int n_nodes, const float* grad, const float* const* xs,
+                           float* const* outs, int64_t n, c3cu_stream_t stream);
+
 int c3cu_convert(const void* in, int in_dtype, void* out, int out_dtype, int64_t n,
                  c3cu_stream_t stream);
 

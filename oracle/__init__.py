@@ -205,3 +205,19 @@ def mlp_train_step(params, x, y, lr):
     g["b1"] = sum_reduce(dz1, 0)
     new = {k: sgd(params[k], g[k], lr) for k in params}
     return loss, z3, g, new
+
+
+BW_OPS = {"ReLU": 1, "Sigmoid": 2, "Tanh": 3, "Neg": 4, "Exp": 5, "Log": 6}
+
+
+def backward_chain(types, grad, xs):
+    """Gradients each node of a unary elementwise chain passes upstream (see c3_oracle.c)."""
+    grad = np.ascontiguousarray(grad, dtype=np.float32).ravel()
+    n = grad.size
+    ops = (ctypes.c_int * len(types))(*[BW_OPS[t] for t in types])
+    xs = [None if x is None else np.ascontiguousarray(x, dtype=np.float32).ravel() for x in xs]
+    xp = (_f32p * len(types))(*[_null() if x is None else _f(x) for x in xs])
+    outs = [np.empty(n, dtype=np.float32) for _ in types]
+    op = (_f32p * len(types))(*[_f(o) for o in outs])
+    lib().c3o_backward_chain(ops, len(types), _f(grad), xp, op, n)
+    return outs

@@ -340,3 +340,42 @@ C3O_EXPORT void c3o_softmax_ce(const float* z, const int32_t* y, float* loss, fl
 C3O_EXPORT void c3o_sgd(float* p, const float* g, size_t n, float lr) {
   for (size_t i = 0; i < n; ++i) p[i] = p[i] - lr * g[i];
 }
+
+/* ------------------------------------------------------------------ fused backward chains
+ * The gradient graphs the reference builds per unary node (src/C3/C3BackwardCapture.cpp:
+ * 501-617 ReLU/Sigmoid/Tanh, 725-743 Neg, 823-872 Exp/Log), chained from the most
+ * downstream node (k = 0) upstream as the fused sequence kernel does (:1133-1210); each
+ * graph node is one IEEE fp32 operation (the fused graphs compile without secondary fusion,
+ * :1236-1246). ops: 1 ReLU, 2 Sigmoid, 3 Tanh, 4 Neg, 5 Exp, 6 Log. outs[k] = the gradient
+ * node k passes upstream. */
+C3O_EXPORT void c3o_backward_chain(const int* ops, int n_nodes, const float* grad, const float* const* xs,
+                                   float* const* outs, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    float g = grad[i];
+    for (int k = 0; k < n_nodes; ++k) {
+      const float x = xs[k] ? xs[k][i] : 0.f;
+      float r;
+      switch (ops[k]) {
+        case 1: r = (x > 0.f ? 1.f : 0.f) * g; break;
+        case 2: {
+          const float e = expf(-x);
+          const float s = 1.f / (1.f + e);
+          r = g * (s * (1.f - s));
+          break;
+        }
+        case 3: {
+          const float ep = expf(x), en = expf(-x);
+          const float t = (ep - en) / (ep + en);
+          r = g * (1.f - t * t);
+          break;
+        }
+        case 4: r = -g; break;
+        case 5: r = expf(x) * g; break;
+        case 6: r = g / x; break;
+        default: r = NAN; break;
+      }
+      outs[k][i] = r;
+      g = r;
+    }
+  }
+}

@@ -35,6 +35,8 @@ void c3o_matmul(const float* A, const float* B, float* out, size_t M, size_t K, 
                 int transB, const float* bias, size_t bias_numel, int act, size_t r0, size_t r1, int threads);
 void c3o_relu_bwd(const float* grad, const float* x, float* out, size_t n);
 void c3o_sum_reduce(const float* in, float* out, size_t M, size_t N, int axis);
+void c3o_backward_chain(const int* ops, int n_nodes, const float* grad, const float* const* xs, float* const* outs,
+                        size_t n);
 }
 
 // Graph node structs and the host framework's autograd node classes share names
@@ -303,6 +305,29 @@ TEST(backward_keys_and_disabled_device_path, false) {
   CHECK(C3BackwardCapture::supportsNodeType("10MatMulNode") && !C3BackwardCapture::supportsNodeType("Foo"));
 }
 
+TEST(fused_backward_sequence_detection, false) {
+  auto& bc = C3BackwardCapture::getInstance();
+  bc.clear();
+  const std::vector<size_t> shp{32, 64};
+  Tensor x(ShapeTag{}, shp, DType::kFloat, DeviceType::kCPU);
+  const std::string sig = typeid(::SigmoidNode).name(), tanh_t = typeid(::TanhNode).name(),
+                    mm = typeid(::MatMulNode).name();
+  // backward order of y = sigmoid(tanh(x)): Sigmoid first, then Tanh
+  bc.recordBackwardNode(sig, shp, shp, {x});
+  bc.recordBackwardNode(tanh_t, shp, shp, {x});
+  bc.recordBackwardNode(mm, shp, shp, {x});  // not elementwise: never enters the window
+  bc.waitForPendingCompiles();
+  const std::string key = C3BackwardCapture::makeFusedBackwardKey("Sigmoid+Tanh", shp, shp);
+  CHECK(key == "backward_fused_Sigmoid+Tanh|g:32,64,|i:32,64,");
+  CHECK(C3KernelRegistry::getInstance().hasBackwardKey(key));
+  CHECK(bc.getStats().fusion_compile_count >= 1);
+  CHECK(C3BackwardCapture::makeSequenceKey({sig, tanh_t, typeid(::ReLUNode).name()}) == "Sigmoid+Tanh+ReLU");
+  CHECK(!C3BackwardCapture::isFusableSequence({sig}));
+  CHECK(!C3BackwardCapture::isFusableSequence({sig, mm}));
+  CHECK(C3BackwardCapture::isElementWiseBackward(typeid(::ExpNode).name()) &&
+        !C3BackwardCapture::isElementWiseBackward(typeid(::AddNode).name()));
+}
+
 // ============================================================================ GPU
 TEST(gpu_region_fp32_is_bit_exact_through_registry, true) {
   // cfg1 layer shapes: the fp32 path reproduces the reference's loop arithmetic exactly.
@@ -398,6 +423,58 @@ TEST(gpu_region_bf16_device_tensors, true) {
     max_ref = std::max(max_ref, (double)std::fabs(ref[i]));
   }
   CHECK(max_err / max_ref <= 2e-2);
+  uint32_t fault = 0;
+  CHECK(c3cu_fault_status(&fault) == 0 && fault == 0);
+}
+
+TEST(gpu_fused_backward_chain_intercepts, true) {
+  // y = Sigmoid(Tanh(Exp(x))): backward visits Sigmoid, Tanh, Exp. After one recorded pass the
+  // fused kernel runs once at Sigmoid and hands Tanh and Exp their gradients (path A).
+  auto& bc = C3BackwardCapture::getInstance();
+  bc.clear();
+  std::mt19937 rng(21);
+  const size_t R = 64, C = 96, n = R * C;
+  Tensor x0 = hostTensor({R, C}, rng, -1.5f, 1.5f);  // Exp input
+  Tensor x1 = hostTensor({R, C}, rng, -2.f, 2.f);    // Tanh input
+  Tensor x2 = hostTensor({R, C}, rng, -3.f, 3.f);    // Sigmoid input
+  Tensor grad = hostTensor({R, C}, rng, -1.f, 1.f);
+  auto exp_n = std::make_shared<::ExpNode>(std::vector<Tensor>{x0});
+  auto tanh_n = std::make_shared<::TanhNode>(std::vector<Tensor>{x1});
+  auto wrap = std::make_shared<::FactorNode>(std::vector<Tensor>{x1});
+  wrap->setUpStreamNodes({exp_n});
+  tanh_n->setUpStreamNodes({wrap});  // a wrapper between two elementwise nodes is skipped
+  auto sig_n = std::make_shared<::SigmoidNode>(std::vector<Tensor>{x2});
+  sig_n->setUpStreamNodes({tanh_n});
+  for (auto* t : {typeid(::SigmoidNode).name(), typeid(::TanhNode).name(), typeid(::ExpNode).name()})
+    bc.recordBackwardNode(t, {R, C}, {R, C}, {x0});
+  bc.waitForPendingCompiles();
+  auto g0 = bc.tryExecuteFusedBackward(sig_n.get(), grad, {x2});
+  CHECK(g0.has_value());
+  auto g1 = bc.tryExecuteFusedBackward(tanh_n.get(), grad, {x1});  // grad is ignored: intercepted
+  auto g2 = bc.tryExecuteFusedBackward(exp_n.get(), grad, {x0});
+  CHECK(g1.has_value() && g2.has_value());
+  std::vector<float> r0(n), r1(n), r2(n);
+  const int ops[3] = {C3CU_BW_SIGMOID, C3CU_BW_TANH, C3CU_BW_EXP};
+  const float* xs[3] = {x2.data_read<float>(), x1.data_read<float>(), x0.data_read<float>()};
+  float* outs[3] = {r0.data(), r1.data(), r2.data()};
+  c3o_backward_chain(ops, 3, grad.data_read<float>(), xs, outs, n);
+  auto close = [&](const Tensor& t, const std::vector<float>& ref) {
+    double worst = 0, scale = 0;
+    for (size_t i = 0; i < n; ++i) {
+      worst = std::max(worst, (double)std::fabs(t.data_read<float>()[i] - ref[i]));
+      scale = std::max(scale, (double)std::fabs(ref[i]));
+    }
+    return worst <= 1e-5 * scale;
+  };
+  CHECK(g0 && close(*g0, r0));
+  CHECK(g1 && close(*g1, r1));
+  CHECK(g2 && close(*g2, r2));
+  CHECK(bc.getStats().fusion_hit_count >= 3);
+  // a node outside any compiled chain misses once, then is remembered as a miss
+  auto lone = std::make_shared<::NegNode>(std::vector<Tensor>{x0});
+  CHECK(!bc.tryExecuteFusedBackward(lone.get(), grad, {x0}).has_value());
+  CHECK(!bc.tryExecuteFusedBackward(lone.get(), grad, {x0}).has_value());
+  bc.clearInterceptedState();
   uint32_t fault = 0;
   CHECK(c3cu_fault_status(&fault) == 0 && fault == 0);
 }

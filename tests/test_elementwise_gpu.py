@@ -126,3 +126,61 @@ def test_sum_rows(cuda_device, M, N):
     out2 = ew.sum_rows(x.to(cuda_device))
     torch.cuda.synchronize()
     assert torch.equal(out.cpu(), out2.cpu())
+
+
+CHAINS = [["ReLU", "ReLU"], ["Sigmoid", "Tanh"], ["ReLU", "Sigmoid", "Tanh"], ["Tanh", "Exp", "Log", "Neg"],
+          ["Neg", "ReLU", "Neg"], ["Sigmoid", "Sigmoid", "Sigmoid", "Sigmoid"], ["Exp", "Tanh"]]
+
+
+@pytest.mark.parametrize("types", CHAINS, ids=["+".join(c) for c in CHAINS])
+@pytest.mark.parametrize("n", [1, 4097, 1 << 20])
+def test_backward_chain_parity(cuda_device, types, n):
+    """Fused backward of a unary chain against the oracle's node-by-node gradients: exact for
+    ReLU / Neg chains; otherwise within 1e-5 relative plus a floor of 1e-6 of the tensor's
+    largest value (1 - s and 1 - t^2 cancel when s or |t| is near 1)."""
+    g = torch.Generator().manual_seed(n + len(types))
+    grad = torch.randn(n, generator=g)
+    xs = []
+    for t in types:
+        x = torch.randn(n, generator=g) * 2
+        if t == "Log":
+            x = x.abs() + 0.25
+        xs.append(None if t == "Neg" else x)
+    outs = ew.backward_chain(types, grad.to(cuda_device), [None if x is None else x.to(cuda_device) for x in xs])
+    torch.cuda.synchronize()
+    refs = oracle.backward_chain(types, grad.numpy(), [None if x is None else x.numpy() for x in xs])
+    exact = all(t in ("ReLU", "Neg") for t in types)
+    for k, (o, r) in enumerate(zip(outs, refs)):
+        o = o.cpu().numpy()
+        if exact:
+            assert np.array_equal(o, r), f"node {k}"
+        else:
+            bound = 1e-5 * np.abs(r) + 1e-6 * np.abs(r).max()
+            assert (np.abs(o - r) <= bound).all(), f"node {k}: max err {np.abs(o - r).max():.3e}"
+
+
+def test_program_multi_output(cuda_device):
+    """Two outputs from one pass: (a + b) and (a + b) * c."""
+    n = 10000
+    a, b, c = (torch.randn(n, generator=torch.Generator().manual_seed(s)) for s in (1, 2, 3))
+    import ctypes
+    from c3_b200 import _lib
+    from c3_b200.linear import _p, _stream
+    ins = [t.to(cuda_device) for t in (a, b, c)]
+    o1, o2 = torch.empty(n, device=cuda_device), torch.empty(n, device=cuda_device)
+    ptrs = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in ins])
+    nums = (ctypes.c_int64 * 3)(n, n, n)
+    code = bytes([ew.ADD, 3, 0, 1, ew.MUL, 4, 3, 2])
+    cbuf = (ctypes.c_uint8 * len(code))(*code)
+    regs = (ctypes.c_int * 2)(3, 4)
+    outs = (ctypes.c_void_p * 2)(o1.data_ptr(), o2.data_ptr())
+    consts = (ctypes.c_float * 1)(0.0)
+    rc = _lib.load().c3cu_ew_program_multi(ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(nums, ctypes.c_void_p), 3,
+                                           ctypes.cast(cbuf, ctypes.c_void_p), 2, ctypes.cast(consts, ctypes.c_void_p),
+                                           0, ctypes.cast(regs, ctypes.c_void_p), ctypes.cast(outs, ctypes.c_void_p), 2,
+                                           n, _stream(ins[0].device))
+    _lib.check(rc, "c3cu_ew_program_multi")
+    torch.cuda.synchronize()
+    s = (a + b)
+    assert torch.equal(o1.cpu(), s)
+    assert torch.equal(o2.cpu(), s * c)
