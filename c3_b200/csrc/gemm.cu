@@ -2,6 +2,7 @@
 // Linear+bias+ReLU forward, the dX / dW backward GEMMs and the general bf16 GEMM.
 #include <atomic>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <utility>
 
@@ -19,6 +20,18 @@ using gemm::Params;
 // Upper bound on the persistent GEMM's CTAs (0 = one per SM). Lowering it leaves SMs free
 // for a collective that runs concurrently (e.g. an all-reduce overlapped with the dX GEMM).
 std::atomic<int> g_max_ctas{0};
+
+// Per-shape variants chosen by a tuner (c3cu_gemm_tune_set); they take precedence over
+// g_variant for an exact (M, N, K, majors, epilogue) match.
+struct TuneKey {
+  int64_t M, N, K;
+  int a_mn, b_mn, epi;
+  bool operator<(const TuneKey& o) const {
+    return std::tie(M, N, K, a_mn, b_mn, epi) < std::tie(o.M, o.N, o.K, o.a_mn, o.b_mn, o.epi);
+  }
+};
+std::mutex g_tune_mu;
+std::map<TuneKey, int> g_tune;
 
 // Kernel variant: 0 = automatic (the CTA-pair kernel whenever M spans at least two 128-row
 // halves, with the split-K tail), 1 = single-CTA kernel only, 2 = CTA-pair kernel whenever it
@@ -86,7 +99,7 @@ int split_workspace(cudaStream_t stream, float** partial, uint32_t** tickets, ui
 
 template <bool A_MN, bool B_MN, int EPI>
 int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
-                cudaStream_t stream) {
+                cudaStream_t stream, int variant) {
   CUtensorMap ta, tb;
   int rc;
   // Per CTA: A 128 (M) x 64 (K), B 128 (N) x 64 (K); MN-major operands in 64 x 64 boxes.
@@ -125,7 +138,7 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   q.sk_mode = 0;
   q.sk_first = 0;
   const int k_blocks = (p.K + gemm2::BK - 1) / gemm2::BK;
-  if (g_variant.load(std::memory_order_relaxed) == 0 && k_blocks >= 64) {
+  if (variant == 0 && k_blocks >= 64) {
     const int tail = tiles % clusters;
     if (tail > 0 && 2 * tail <= clusters) {
       q.sk_mode = 1;
@@ -185,11 +198,18 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
 
 int dispatch(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
              int epi, const Params& p, cudaStream_t st) {
-  const int variant = g_variant.load(std::memory_order_relaxed);
+  int variant = g_variant.load(std::memory_order_relaxed);
+  {
+    std::lock_guard<std::mutex> lock(g_tune_mu);
+    if (!g_tune.empty()) {
+      auto it = g_tune.find(TuneKey{p.M, p.N, p.K, a_mn, b_mn, epi});
+      if (it != g_tune.end()) variant = it->second;
+    }
+  }
   const bool pair = variant != 1 && p.M > gemm2::HM;
 #define C3CU_GEMM_CASE(AM, BMN, E)                                          \
   if (a_mn == AM && b_mn == BMN && epi == E)                                \
-    return pair ? launch_pair<AM, BMN, E>(A, lda, B, ldb, p, st)            \
+    return pair ? launch_pair<AM, BMN, E>(A, lda, B, ldb, p, st, variant)   \
                 : launch<AM, BMN, E>(A, lda, B, ldb, p, st);
   C3CU_GEMM_CASE(0, 0, kEpiBiasReluMask)
   C3CU_GEMM_CASE(0, 1, kEpiBiasReluMask)
@@ -284,6 +304,22 @@ int c3cu_set_gemm_variant(int variant) {
     return C3CU_ERR_INVALID;
   }
   c3cu::g_variant.store(variant, std::memory_order_relaxed);
+  return C3CU_OK;
+}
+
+int c3cu_gemm_tune_set(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int epilogue, int variant) {
+  if (variant < 0 || variant > 2 || M < 0 || N < 0 || K < 0) {
+    c3cu::set_error("gemm_tune_set: bad arguments (variant %d)", variant);
+    return C3CU_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(c3cu::g_tune_mu);
+  c3cu::g_tune[c3cu::TuneKey{M, N, K, a_mn, b_mn, epilogue}] = variant;
+  return C3CU_OK;
+}
+
+int c3cu_gemm_tune_clear(void) {
+  std::lock_guard<std::mutex> lock(c3cu::g_tune_mu);
+  c3cu::g_tune.clear();
   return C3CU_OK;
 }
 

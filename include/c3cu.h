@@ -134,6 +134,11 @@ int c3cu_set_gemm_max_ctas(int max_ctas);
  * and 2 give identical bits (the same K order); on split tiles variant 0 accumulates the two
  * K halves separately, so it differs from them within the fp32 accumulation error bound. */
 int c3cu_set_gemm_variant(int variant);
+/* Per-shape variant table filled by a tuner (the B200 counterpart of the reference's tile
+ * auto-tuner, include/C3/AutoTuner.h:42-63, src/C3/C3Engine.cpp:1577-1651): calls of exactly
+ * (M, N, K, a_mn, b_mn, epilogue) use `variant` instead of the process-wide one. */
+int c3cu_gemm_tune_set(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int epilogue, int variant);
+int c3cu_gemm_tune_clear(void);
 
 /* ------------------------------------------------------------------ exact fp32 (CUDA cores)
  * Bit-exact restatements of the reference's fp32 loops: every output element is reduced

@@ -261,3 +261,23 @@ def test_gemm_variants_agree(cuda_device, gemm_variant, M, N, K):
     if diff.any():
         y = np.maximum(np.abs(f32(Y0)), np.abs(f32(Y1)))[diff]
         assert y.max() <= 1e-4 * float(np.abs(f32(Y1)).max()), "mask flip away from zero"
+
+
+def test_tuner_picks_and_applies_a_variant(cuda_device, tmp_path):
+    """tune_gemm times the three variants, installs the fastest per shape and persists it; a
+    GEMM then runs through the table with the same results as before (within bf16)."""
+    from c3_b200 import _lib, tuning
+    M, N, K = 1024, 512, 4096
+    X, W, b = _fwd_inputs(M, N, K, 5, cuda_device)
+    Y0, _ = linear.forward(X, W, b, "nk")
+    entries = tuning.tune_gemm([(M, N, K, 0, 0, 0)], iters=3, path=tmp_path / "t.json")
+    try:
+        (e,) = entries.values()
+        assert e["variant"] in (0, 1, 2) and set(e["us"]) == {"0", "1", "2"}
+        assert tuning.read(tmp_path / "t.json")["entries"].keys() == entries.keys()
+        Y1, _ = linear.forward(X, W, b, "nk")
+        torch.cuda.synchronize()
+        a, c = f32(Y1), f32(Y0)
+        assert (np.abs(a - c) <= 2.0 ** -7 * np.maximum(np.abs(a), np.abs(c)) + 1e-5 * np.abs(c).max()).all()
+    finally:
+        _lib.load().c3cu_gemm_tune_clear()
