@@ -317,6 +317,18 @@ int c3cu_gemm_tune_set(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int 
   return C3CU_OK;
 }
 
+int c3cu_gemm_tune_get(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int epilogue, int* variant) {
+  if (!variant) return C3CU_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(c3cu::g_tune_mu);
+  auto it = c3cu::g_tune.find(c3cu::TuneKey{M, N, K, a_mn, b_mn, epilogue});
+  if (it == c3cu::g_tune.end()) {
+    c3cu::set_error("gemm_tune_get: no entry for this shape");
+    return C3CU_ERR_INVALID;
+  }
+  *variant = it->second;
+  return C3CU_OK;
+}
+
 int c3cu_gemm_tune_clear(void) {
   std::lock_guard<std::mutex> lock(c3cu::g_tune_mu);
   c3cu::g_tune.clear();

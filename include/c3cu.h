@@ -138,6 +138,7 @@ int c3cu_set_gemm_variant(int variant);
  * auto-tuner, include/C3/AutoTuner.h:42-63, src/C3/C3Engine.cpp:1577-1651): calls of exactly
  * (M, N, K, a_mn, b_mn, epilogue) use `variant` instead of the process-wide one. */
 int c3cu_gemm_tune_set(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int epilogue, int variant);
+int c3cu_gemm_tune_get(int64_t M, int64_t N, int64_t K, int a_mn, int b_mn, int epilogue, int* variant);
 int c3cu_gemm_tune_clear(void);
 
 /* ------------------------------------------------------------------ exact fp32 (CUDA cores)

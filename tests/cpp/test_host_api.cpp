@@ -479,6 +479,59 @@ TEST(gpu_fused_backward_chain_intercepts, true) {
   CHECK(c3cu_fault_status(&fault) == 0 && fault == 0);
 }
 
+TEST(gpu_two_tier_matmul_tuned_tier, true) {
+  // opt 2 (precompiled) and opt 4 (tuned) bind the same GEMM; the first run of the opt-4
+  // kernel times the variants for its shape and installs the fastest, the registry keeps
+  // the higher level, and both tiers agree to bf16 rounding.
+  c3cu_gemm_tune_clear();
+  const size_t M = 512, K = 1024, N = 768;
+  std::mt19937 rng(31);
+  Tensor A = hostTensor({M, K}, rng, -1, 1), B = hostTensor({K, N}, rng, -0.05f, 0.05f);
+  auto bf16Dev = [](const Tensor& t) {
+    Tensor d = t.to(DeviceType::kCUDA);
+    Tensor o(ShapeTag{}, t.shape(), DType::kBF16, DeviceType::kCUDA);
+    c3cu_convert(d.data(), C3CU_DTYPE_F32, o.data(), C3CU_DTYPE_BF16, t.numel(), ct::c3::cuda::currentStream());
+    return o;
+  };
+  Tensor Ad = bf16Dev(A), Bd = bf16Dev(B);
+  Graph g;
+  auto a = TensorDesc::fromShape({M, K}), b = TensorDesc::fromShape({K, N}), o = TensorDesc::fromShape({M, N});
+  const size_t ai = g.addInput(a), bi = g.addInput(b);
+  g.markOutput(g.addNode(c3::MatMulNode{a, b}, {ai, bi}, o));
+  c3::CompileOptions fast, tuned;
+  fast.opt_level = 2;
+  tuned.opt_level = 4;
+  auto k2 = C3Engine::getInstance().compile(g, fast);
+  auto k4 = C3Engine::getInstance().compile(g, tuned);
+  CHECK(k2 && k4 && k2->optLevel() == 2 && k4->optLevel() == 4);
+  auto& reg = C3KernelRegistry::getInstance();
+  reg.uninstallAll();
+  KernelShapeInfo info{{M, K}, {K, N}, {M, N}, true, M, K, N, ""};
+  reg.install(op::MatMul, DeviceType::kCUDA, k4, info);
+  reg.install(op::MatMul, DeviceType::kCUDA, k2, info);  // lower level: the tuned tier stays
+  auto y4 = k4->execute({Ad, Bd});
+  int variant = -1;
+  // B [K, N] is read MN-major (b_mn = 1) by the bf16 GEMM, A K-major; bf16 output
+  CHECK(c3cu_gemm_tune_get(M, N, K, 0, 1, C3CU_EPI_STORE_BF16, &variant) == 0 && variant >= 0 && variant <= 2);
+  auto y2 = k2->execute({Ad, Bd});
+  auto toF32 = [](const Tensor& t) {
+    Tensor f(ShapeTag{}, t.shape(), DType::kFloat, DeviceType::kCUDA);
+    c3cu_convert(t.data(), C3CU_DTYPE_BF16, f.data(), C3CU_DTYPE_F32, t.numel(), ct::c3::cuda::currentStream());
+    return f.to(DeviceType::kCPU);
+  };
+  Tensor h4 = toF32(y4[0]), h2 = toF32(y2[0]);
+  double worst = 0, scale = 0;
+  for (size_t i = 0; i < M * N; ++i) {
+    worst = std::max(worst, (double)std::fabs(h4.data_read<float>()[i] - h2.data_read<float>()[i]));
+    scale = std::max(scale, (double)std::fabs(h2.data_read<float>()[i]));
+  }
+  CHECK(worst <= 2e-2 * scale);
+  reg.uninstallAll();
+  c3cu_gemm_tune_clear();
+  uint32_t fault = 0;
+  CHECK(c3cu_fault_status(&fault) == 0 && fault == 0);
+}
+
 int main(int argc, char** argv) {
   const bool gpu = argc > 1 && std::string(argv[1]) == "--gpu";
   int ran = 0;
