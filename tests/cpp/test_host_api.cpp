@@ -428,8 +428,10 @@ TEST(gpu_region_bf16_device_tensors, true) {
 }
 
 TEST(gpu_fused_backward_chain_intercepts, true) {
-  // y = Sigmoid(Tanh(Exp(x))): backward visits Sigmoid, Tanh, Exp. After one recorded pass the
-  // fused kernel runs once at Sigmoid and hands Tanh and Exp their gradients (path A).
+  // y = Sigmoid(Tanh(Exp(x))): backward visits Sigmoid, Tanh, Exp. The recording window counts
+  // a complete two-node chain and then restarts (src/C3/C3BackwardCapture.cpp:886-931), so the
+  // compiled sequence is the pair Sigmoid+Tanh: the fused kernel runs once at Sigmoid, Tanh
+  // receives its gradient from the intercept table (path A), and Exp stays on the host's path.
   auto& bc = C3BackwardCapture::getInstance();
   bc.clear();
   std::mt19937 rng(21);
@@ -452,7 +454,7 @@ TEST(gpu_fused_backward_chain_intercepts, true) {
   CHECK(g0.has_value());
   auto g1 = bc.tryExecuteFusedBackward(tanh_n.get(), grad, {x1});  // grad is ignored: intercepted
   auto g2 = bc.tryExecuteFusedBackward(exp_n.get(), grad, {x0});
-  CHECK(g1.has_value() && g2.has_value());
+  CHECK(g1.has_value() && !g2.has_value());
   std::vector<float> r0(n), r1(n), r2(n);
   const int ops[3] = {C3CU_BW_SIGMOID, C3CU_BW_TANH, C3CU_BW_EXP};
   const float* xs[3] = {x2.data_read<float>(), x1.data_read<float>(), x0.data_read<float>()};
@@ -468,8 +470,11 @@ TEST(gpu_fused_backward_chain_intercepts, true) {
   };
   CHECK(g0 && close(*g0, r0));
   CHECK(g1 && close(*g1, r1));
-  CHECK(g2 && close(*g2, r2));
-  CHECK(bc.getStats().fusion_hit_count >= 3);
+  CHECK(bc.getStats().fusion_hit_count >= 2);
+  CHECK(C3KernelRegistry::getInstance().hasBackwardKey(
+      C3BackwardCapture::makeFusedBackwardKey("Sigmoid+Tanh", {R, C}, {R, C})));
+  CHECK(!C3KernelRegistry::getInstance().hasBackwardKey(
+      C3BackwardCapture::makeFusedBackwardKey("Sigmoid+Tanh+Exp", {R, C}, {R, C})));
   // a node outside any compiled chain misses once, then is remembered as a miss
   auto lone = std::make_shared<::NegNode>(std::vector<Tensor>{x0});
   CHECK(!bc.tryExecuteFusedBackward(lone.get(), grad, {x0}).has_value());
