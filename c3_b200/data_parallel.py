@@ -255,10 +255,11 @@ class LinearReluTrainStep:
 def default_overlap(world: int) -> tuple[int, int]:
     """(CTAs of the in-switch all-reduce, SMs left free for it during the dX GEMM).
 
-    Measured on 8 B200s (cfg3, 2048 rows per rank): 20 CTAs on 20 reserved SMs gave the
-    shortest step (the all-reduce otherwise competes with the dX GEMM's CTAs); with 2 ranks
-    the dX GEMM is long enough to hide the all-reduce, and every SM goes to the GEMM."""
-    return (20, 20) if world >= 8 else (16, 0)
+    Measured on B200s (cfg3): 20 CTAs on 20 reserved SMs gave the shortest step with 2 ranks
+    (2722 TFLOP/s, against 2370 with no reserve and 16 CTAs) and with 8 ranks (5396 against
+    4983). Without a reserve, the all-reduce competes with the CTA-pair dX GEMM's CTAs and
+    runs about twice as long."""
+    return (20, 20) if world > 1 else (16, 0)
 
 
 def env_grad_dtype() -> torch.dtype:
