@@ -132,7 +132,10 @@ int c3cu_set_gemm_max_ctas(int max_ctas);
  * tiles are split in two K halves whose fp32 partial sums are added once, K-half order
  * fixed), 1 = single-CTA kernel only, 2 = CTA-pair kernel without the K split. Variants 1
  * and 2 give identical bits (the same K order); on split tiles variant 0 accumulates the two
- * K halves separately, so it differs from them within the fp32 accumulation error bound. */
+ * K halves separately, so it differs from them within the fp32 accumulation error bound.
+ * The first split launch on a (device, stream) allocates a 21 MB workspace (fp32 partials and
+ * tickets) that the library keeps for that stream; capture such a launch in a CUDA graph only
+ * after one uncaptured call on the same stream. */
 int c3cu_set_gemm_variant(int variant);
 /* Per-shape variant table filled by a tuner (the B200 counterpart of the reference's tile
  * auto-tuner, include/C3/AutoTuner.h:42-63, src/C3/C3Engine.cpp:1577-1651): calls of exactly
