@@ -13,8 +13,10 @@
 //               the S buffer; O is rescaled in TMEM only when the running maximum grows by
 //               more than 2^8 (lazy rescaling), and normalised by the row sum at the end
 // TMEM: S buffers at columns [0,128) and [128,256), O at [256,384) (512 allocated).
-// The default launch is flash_fwd2_kernel (attn2.cuh): two query tiles per CTA sharing each
-// K / V block, with ping-pong softmax warpgroups; this single-tile kernel is variant 1.
+// The default launch is flash_fwd3_kernel (attn3.cuh): two query tiles per CTA sharing each
+// 64-key K / V block, two S buffers per tile, ping-pong softmax warpgroups. flash_fwd2_kernel
+// (attn2.cuh, 128-key blocks, one S buffer per tile) is variant 2 and this single-tile kernel
+// variant 1.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -348,15 +350,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace c3cu
 
 #include "attn2.cuh"
+#include "attn3.cuh"
 
 namespace c3cu {
 namespace attn {
 
-// 0 = automatic (two query tiles per CTA), 1 = one query tile per CTA.
+// 0 = automatic (= 3), 1 = one query tile per CTA, 2 = two query tiles with 128-key blocks,
+// 3 = two query tiles with 64-key blocks and two S buffers per tile.
 static int g_attn_variant = 0;
 
 namespace {
-int encode_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S) {
+int encode_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S, uint32_t box_rows = 128) {
   if (!aligned16(base)) {
     set_error("flash_attn_fwd: tensor base %p is not 16-byte aligned", base);
     return C3CU_ERR_ALIGN;
@@ -374,7 +378,7 @@ int encode_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S) {
   }
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(HD), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(HD) * 2, static_cast<cuuint64_t>(S) * HD * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -448,6 +452,19 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
+  if (attn::g_attn_variant == 0 || attn::g_attn_variant == 3) {
+    // 64-key blocks: K / V tensor maps with 64-row boxes
+    CUtensorMap tk64, tv64;
+    if ((rc = attn::encode_bhsd(&tk64, K, B * H, S, 64)) != C3CU_OK) return rc;
+    if ((rc = attn::encode_bhsd(&tv64, V, B * H, S, 64)) != C3CU_OK) return rc;
+    rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          attn::SMEM_BYTES3),
+                     "flash_attn_fwd: set shared memory");
+    if (rc != C3CU_OK) return rc;
+    attn::flash_fwd3_kernel<<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
+                              static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
+    return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+  }
   auto go = [&](auto kern) -> int {
     int r = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              attn::SMEM_BYTES2),
@@ -461,7 +478,7 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
 }
 
 extern "C" int c3cu_set_attn_variant(int variant) {
-  if (variant < 0 || variant > 1) {
+  if (variant < 0 || variant > 3) {
     c3cu::set_error("set_attn_variant: unknown variant %d", variant);
     return C3CU_ERR_INVALID;
   }

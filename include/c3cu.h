@@ -233,8 +233,9 @@ int c3cu_sum_rows_f32(const float* in, float* out, int64_t M, int64_t N, void* w
 int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, float* LSE,
                         int64_t B, int64_t H, int64_t S, int64_t D, float scale, int causal,
                         c3cu_stream_t stream);
-/* Attention kernel for the calls that follow (process-wide): 0 = two 128-row query tiles per
- * CTA sharing each K / V block (default), 1 = one query tile per CTA. */
+/* Attention kernel for the calls that follow (process-wide): 0 = default (3); 1 = one
+ * 128-row query tile per CTA; 2 = two query tiles per CTA sharing each 128-key K / V block;
+ * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM. */
 int c3cu_set_attn_variant(int variant);
 
 /* ------------------------------------------------------------------ data-parallel collective

@@ -64,21 +64,58 @@ def test_flash_attention_cfg5_full_size_sampled(cuda_device):
         _check(Q, K, V, O, L, True, [(b, h)], rows_per_pair=(r0, r0 + 64))
 
 
+@pytest.mark.parametrize("variant", [0, 2])
 @pytest.mark.parametrize("S,causal", [(384, True), (1024, True), (300, False)])
-def test_flash_attention_kernels_agree(cuda_device, S, causal):
-    """The two-tile kernel (default) and the one-tile kernel (variant 1) agree to bf16
-    rounding: they differ only in the exponentials computed on the FMA pipe (relative error
-    below 1e-4) and the resulting bf16 roundings of P and O."""
+def test_flash_attention_kernels_agree(cuda_device, S, causal, variant):
+    """The two-tile kernels (default 64-key blocks, and variant 2 with 128-key blocks) agree
+    with the one-tile kernel (variant 1) to bf16 rounding: the online softmax visits the keys
+    in different block sizes, so the rescalings and the bf16 roundings of P and O differ."""
     from c3_b200 import _lib
     L = _lib.load()
     Q, K, V = _qkv(1, 4, S, 77 + S, cuda_device)
     try:
         _lib.check(L.c3cu_set_attn_variant(1), "c3cu_set_attn_variant")
         O1, L1 = flash_attn_fwd(Q, K, V, causal=causal)
-        _lib.check(L.c3cu_set_attn_variant(0), "c3cu_set_attn_variant")
+        _lib.check(L.c3cu_set_attn_variant(variant), "c3cu_set_attn_variant")
         O0, L0 = flash_attn_fwd(Q, K, V, causal=causal)
         torch.cuda.synchronize()
     finally:
         L.c3cu_set_attn_variant(0)
     assert_bf16_close(O0.float().cpu().numpy(), O1.float().cpu().numpy(), "O two-tile vs one-tile")
     assert (L0 - L1).abs().max().item() <= 1e-3
+
+
+@pytest.fixture
+def attn_variant():
+    from c3_b200 import _lib
+    L = _lib.load()
+    yield lambda v: _lib.check(L.c3cu_set_attn_variant(v), "c3cu_set_attn_variant")
+    L.c3cu_set_attn_variant(0)
+
+
+@pytest.mark.parametrize("S", [64, 128, 192, 384, 1024, 200, 300])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_attention_64key_blocks(cuda_device, attn_variant, S, causal):
+    """Variant 3 (64-key blocks, two S buffers per tile; the default) against the oracle."""
+    attn_variant(3)
+    B, H = 2, 3
+    Q, K, V = _qkv(B, H, S, 5 * S + int(causal), cuda_device)
+    O, L = flash_attn_fwd(Q, K, V, causal=causal)
+    torch.cuda.synchronize()
+    _check(Q, K, V, O, L, causal, [(0, 0), (1, 2)])
+
+
+def test_flash_attention_64key_blocks_large_values_and_cfg5(cuda_device, attn_variant):
+    attn_variant(3)
+    Q, K, V = _qkv(1, 2, 1024, 9, cuda_device)
+    Q = (Q.float() * 4).to(torch.bfloat16)
+    O, L = flash_attn_fwd(Q, K, V, causal=True)
+    torch.cuda.synchronize()
+    _check(Q, K, V, O, L, True, [(0, 0), (0, 1)])
+    B, H, S = 8, 32, 8192
+    Q, K, V = _qkv(B, H, S, 5, cuda_device)
+    O, L = flash_attn_fwd(Q, K, V, causal=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(O.float()).all()
+    for (b, h, r0) in [(0, 0, 0), (7, 31, S - 64), (3, 17, 4000)]:
+        _check(Q, K, V, O, L, True, [(b, h)], rows_per_pair=(r0, r0 + 64))
