@@ -16,7 +16,7 @@
 namespace c3cu {
 namespace exact {
 
-constexpr int TK = 16;  // k depth of one shared-memory stage
+constexpr int TK = 32;  // k depth of one shared-memory stage
 // Block tile (16 R) x (16 R): 256 threads, R x R outputs each. R = 4 for large outputs;
 // R = 2 or 1 when the 64 x 64 tiles would leave most SMs idle (e.g. the cfg1 layers at
 // batch 128), trading per-thread reuse for parallelism. Every output still accumulates its
@@ -59,17 +59,34 @@ __global__ void __launch_bounds__(256)
       }
       acc[i][j] = init;
     }
-  for (int k0 = 0; k0 < K; k0 += TK) {
-    // 256 threads load TM x 16 of A and 16 x TN of B (R elements each)
+  // 256 threads move TM x TK of A and TK x TN of B per stage (LD elements each of both). The
+  // next stage is fetched into registers while the current one is consumed from shared
+  // memory, so the global-load latency overlaps the k loop.
+  constexpr int LD = TK * 16 * R / 256;
+  float ra[LD], rb[LD];
+  auto fetch = [&](int k0) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
+    for (int r = 0; r < LD; ++r) {
       const int e = threadIdx.x + r * 256;
-      const int am = e / TK, ak = e % TK;  // A tile: [TM][TK]
-      As[ak][am] = load_a<TA, TB>(A, m0 + am, k0 + ak, M, K);
-      const int bk = e / TN, bn = e % TN;  // B tile: [TK][TN]
-      Bs[bk][bn] = load_b<TA, TB>(B, k0 + bk, n0 + bn, K, N);
+      ra[r] = load_a<TA, TB>(A, m0 + e / TK, k0 + e % TK, M, K);  // A tile: [TM][TK]
+      rb[r] = load_b<TA, TB>(B, k0 + e / TN, n0 + e % TN, K, N);  // B tile: [TK][TN]
     }
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int r = 0; r < LD; ++r) {
+      const int e = threadIdx.x + r * 256;
+      As[e % TK][e / TK] = ra[r];
+      Bs[e / TN][e % TN] = rb[r];
+    }
+  };
+  if (K > 0) {
+    fetch(0);
+    stash();
+  }
+  for (int k0 = 0; k0 < K; k0 += TK) {
     __syncthreads();
+    if (k0 + TK < K) fetch(k0 + TK);
     const int kmax = min(TK, K - k0);
     for (int kk = 0; kk < kmax; ++kk) {
       float a[R], b[R];
@@ -83,6 +100,7 @@ __global__ void __launch_bounds__(256)
         for (int j = 0; j < R; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
     }
     __syncthreads();
+    if (k0 + TK < K) stash();
   }
 #pragma unroll
   for (int i = 0; i < R; ++i) {
@@ -120,7 +138,16 @@ __global__ void __launch_bounds__(256)
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= N) return;
   float s = 0.f;
-  for (int i = 0; i < M; ++i) s = __fadd_rn(s, in[(int64_t)i * N + j]);
+  int i = 0;
+  // eight loads in flight, then added in row order (the loads do not depend on the sum)
+  for (; i + 8 <= M; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = in[(int64_t)(i + u) * N + j];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s = __fadd_rn(s, v[u]);
+  }
+  for (; i < M; ++i) s = __fadd_rn(s, in[(int64_t)i * N + j]);
   out[j] = s;
 }
 
