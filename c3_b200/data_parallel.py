@@ -19,6 +19,11 @@ its GEMM ends, overlapped with the remaining bands and with the dX GEMM.
   c3cu_nccl_comm_init), as a C++ host calls it;
 - "group": torch.distributed all_reduce on the process group (NCCL for CUDA tensors, gloo for
   host tensors — the host-side path the CPU tests exercise).
+
+The other paths shard with no exchange at all: the fused forward by rows (`shard_rows`), the
+elementwise chain by vector-aligned element ranges (`shard_range`) and the FlashAttention
+forward by (batch, head) pairs (`shard_heads`). The cfg1 MLP step sums its gradients with one
+all-reduce (c3_b200.mlp.reduce_gradients).
 """
 from __future__ import annotations
 
@@ -39,6 +44,29 @@ def shard_rows(m_global: int, world: int, rank: int) -> tuple[int, int]:
     base, extra = divmod(m_global, world)
     lo = rank * base + min(rank, extra)
     return lo, lo + base + (1 if rank < extra else 0)
+
+
+def shard_range(n: int, world: int, rank: int, align: int = 4) -> tuple[int, int]:
+    """Contiguous elements [lo, hi) of a flat array of n elements (the cfg4 elementwise chain).
+    Every boundary but the last is a multiple of `align` elements (4 fp32 = one 16-byte vector),
+    so every shard starts on a vector boundary when the whole array does; the work is split in
+    whole vectors, the first ranks taking one more where they do not divide evenly."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if n < 0 or align < 1:
+        raise ValueError("negative element count or alignment below 1")
+    vecs = (n + align - 1) // align
+    lo, hi = shard_rows(vecs, world, rank)
+    return min(n, lo * align), min(n, hi * align)
+
+
+def shard_heads(batch: int, heads: int, world: int, rank: int) -> tuple[int, int]:
+    """(batch, head) pairs [lo, hi) of rank `rank`, indexed b * heads + h (the FlashAttention
+    forward: every pair is independent). A [B, H, S, D] tensor viewed as [1, B * H, S, D] gives
+    the shard as the contiguous slice [:, lo:hi]."""
+    if batch < 0 or heads < 0:
+        raise ValueError("negative batch or head count")
+    return shard_rows(batch * heads, world, rank)
 
 
 def dw_bands(n: int, chunks: int, align: int = 8) -> list[tuple[int, int]]:

@@ -15,6 +15,12 @@ textbook definitions.
 Weights use the reference's MatMul layout W [K, N] (fan_in rows). A step is 15 launches on
 the current stream; `capture()` records them once in a CUDA graph so that a step costs one
 graph launch.
+
+Data parallel (one process per GPU): each rank runs the step on its equal share of the global
+batch (`shard_batch`). The gradients and the loss share one flat fp32 buffer, so one all-reduce
+(sum) per step covers them; SGD then uses lr / world and the loss slot is scaled by 1 / world,
+which gives the full-batch mean gradient and mean loss (each rank's loss is already the mean of
+its rows). W and b stay replicated; all ranks apply the same update.
 """
 from __future__ import annotations
 
@@ -22,9 +28,11 @@ import ctypes
 import math
 
 import torch
+import torch.distributed as dist
 
 from . import _lib
 from . import elementwise as ew
+from .data_parallel import shard_rows
 
 LAYERS = (784, 256, 128, 10)
 PARAM_NAMES = ("W1", "b1", "W2", "b2", "W3", "b3")
@@ -53,18 +61,77 @@ def synthetic_batch(seed: int, batch: int = 128, device: torch.device | str = "c
     return x.to(device), y.to(device)
 
 
+def shard_batch(global_batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) of the global batch that rank `rank` trains on. The shares must be equal:
+    each rank's loss is the mean over its own rows, and the sum over ranks is rescaled by
+    1 / world."""
+    if world < 1 or global_batch % world != 0:
+        raise ValueError(f"a global batch of {global_batch} does not split evenly over {world} ranks")
+    return shard_rows(global_batch, world, rank)
+
+
+_SEGMENT_ALIGN = 64  # elements (256 bytes): every gradient view starts on a 256-byte boundary
+
+
+def _segments(shapes: dict) -> list[tuple[int, int]]:
+    """(offset, numel) of each gradient in PARAM_NAMES order, then of the loss."""
+    out, off = [], 0
+    for n in [math.prod(shapes[k]) for k in PARAM_NAMES] + [1]:
+        out.append((off, n))
+        off += (n + _SEGMENT_ALIGN - 1) // _SEGMENT_ALIGN * _SEGMENT_ALIGN
+    return out
+
+
+def flat_numel(shapes: dict) -> int:
+    off, n = _segments(shapes)[-1]
+    return off + n
+
+
+def gradient_views(flat: torch.Tensor, shapes: dict) -> tuple[dict, torch.Tensor]:
+    """Views of one flat fp32 buffer: the gradient of each parameter in PARAM_NAMES order,
+    then the loss (1 element, the buffer's last). Each view starts on a 256-byte boundary;
+    `flat` must hold flat_numel(shapes) elements."""
+    if flat.numel() != flat_numel(shapes) or not flat.is_contiguous():
+        raise ValueError(f"flat buffer holds {flat.numel()} elements, the layout needs {flat_numel(shapes)}")
+    seg = _segments(shapes)
+    views = {k: flat[o:o + n].view(shapes[k]) for k, (o, n) in zip(PARAM_NAMES, seg)}
+    o, n = seg[-1]
+    return views, flat[o:o + n]
+
+
+def reduce_gradients(flat: torch.Tensor, world: int, group=None) -> None:
+    """Sums the gradient + loss buffer over the ranks and turns the loss slot into the mean of
+    the ranks' losses. The gradients stay summed; the update uses `data_parallel_lr`."""
+    if world <= 1:
+        return
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    flat[-1:].mul_(1.0 / world)
+
+
+def data_parallel_lr(lr: float, world: int) -> float:
+    """SGD step on the summed gradients of `world` equal shards (each a mean over its rows)."""
+    return float(lr) / world
+
+
 class MLPTrainStep:
     """One training step of the cfg1 MLP on device-resident fp32 parameters (updated in
-    place). Buffers are allocated once, so a step can be replayed from a CUDA graph."""
+    place). Buffers are allocated once, so a step can be replayed from a CUDA graph.
 
-    def __init__(self, params: dict, batch: int, lr: float = 0.01):
+    `batch` is this process's batch. With `group` (a torch.distributed process group whose
+    size is above 1; dist.group.WORLD for the default one) the step is data parallel: the
+    gradients and the loss are summed over the group before the update."""
+
+    def __init__(self, params: dict, batch: int, lr: float = 0.01, group=None):
         self.p = params
         for k in PARAM_NAMES:
             t = params[k]
             if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
                 raise _lib.C3CUError(-1, "MLPTrainStep", f"{k}: expected a contiguous fp32 CUDA tensor")
         self.B = batch
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
         self.lr = float(lr)
+        self.lr_step = data_parallel_lr(lr, self.world)
         dev = params["W1"].device
         self.device = dev
         d0, d1, d2, d3 = LAYERS
@@ -72,10 +139,12 @@ class MLPTrainStep:
         self.a1, self.z1 = f(batch, d1), f(batch, d1)
         self.a2, self.z2 = f(batch, d2), f(batch, d2)
         self.z3, self.dz3 = f(batch, d3), f(batch, d3)
-        self.loss = f(1)
         self.da2, self.dz2 = f(batch, d2), f(batch, d2)
         self.da1, self.dz1 = f(batch, d1), f(batch, d1)
-        self.g = {k: torch.empty_like(params[k]) for k in PARAM_NAMES}
+        # gradients and loss in one buffer: one all-reduce covers them under data parallelism
+        shapes = {k: tuple(params[k].shape) for k in PARAM_NAMES}
+        self.flat = torch.zeros(flat_numel(shapes), dtype=torch.float32, device=dev)
+        self.g, self.loss = gradient_views(self.flat, shapes)
         n = len(PARAM_NAMES)
         self._pp = (ctypes.c_void_p * n)(*[params[k].data_ptr() for k in PARAM_NAMES])
         self._gp = (ctypes.c_void_p * n)(*[self.g[k].data_ptr() for k in PARAM_NAMES])
@@ -136,10 +205,12 @@ class MLPTrainStep:
         ew.program([self.z1, self.da1], _RELU_BWD, [0.0], 3, B * d1, out=self.dz1)
         self._mm(x, self.dz1, g["W1"], d0, B, d1, 1, 0)
         self._colsum(self.dz1, g["b1"], B, d1)
+        # the one exchange step under data parallelism (NCCL for CUDA tensors)
+        reduce_gradients(self.flat, self.world, self.group)
         # update
         rc = _lib.load().c3cu_sgd_f32(ctypes.cast(self._pp, ctypes.c_void_p), ctypes.cast(self._gp, ctypes.c_void_p),
                                       ctypes.cast(self._np, ctypes.c_void_p), len(PARAM_NAMES),
-                                      ctypes.c_float(self.lr), self._stream())
+                                      ctypes.c_float(self.lr_step), self._stream())
         _lib.check(rc, "c3cu_sgd_f32")
         return self.loss
 

@@ -4,14 +4,18 @@ gradient sum over a world_size-2 gloo process group (c3_b200.data_parallel.Gradi
 region (src/C3/C3BackwardCapture.cpp:501-528, 618-644, 681-723). Each rank's local gradients
 come from the oracle on its rows; the test checks that the sharding and the banded sums
 reassemble the full-batch gradients. A rank that leaves before the exchange makes the other
-rank's sum end with an error instead of hanging it."""
+rank's sum end with an error instead of hanging it.
+
+Also: the exchange-free shards of the elementwise chain (element ranges) and of attention
+((batch, head) pairs), and the cfg1 MLP step's gradient exchange (c3_b200.mlp: flat gradient
++ loss buffer, one all-reduce, lr / world) against the oracle's full-batch step."""
 import os
 import socket
 
 import numpy as np
 import pytest
 
-from c3_b200.data_parallel import dw_bands, shard_rows
+from c3_b200.data_parallel import dw_bands, shard_heads, shard_range, shard_rows
 
 
 def _free_port():
@@ -38,6 +42,29 @@ def test_shard_rows_rejects_bad_rank():
         shard_rows(10, 2, 2)
     with pytest.raises(ValueError):
         shard_rows(10, 0, 0)
+
+
+@pytest.mark.parametrize("n,world,align", [(0, 2, 4), (3, 2, 4), (4099, 2, 4), (1 << 28, 8, 4),
+                                           (1001, 3, 4), (17, 8, 4), (100, 3, 1)])
+def test_shard_range_covers_aligned_and_balanced(n, world, align):
+    ranges = [shard_range(n, world, r, align) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0
+    for lo, hi in ranges:
+        assert (lo % align == 0 or lo == n) and lo <= hi  # an empty last shard sits at n
+        assert hi % align == 0 or hi == n
+    vecs = [(hi - lo + align - 1) // align for lo, hi in ranges]
+    assert max(vecs) - min(vecs) <= 1
+
+
+@pytest.mark.parametrize("b,h,world", [(8, 32, 8), (8, 32, 3), (1, 2, 4), (0, 4, 2)])
+def test_shard_heads_cover_all_pairs(b, h, world):
+    ranges = [shard_heads(b, h, world, r) for r in range(world)]
+    covered = [i for lo, hi in ranges for i in range(lo, hi)]
+    assert covered == list(range(b * h))
+    with pytest.raises(ValueError):
+        shard_range(8, 2, 2)
 
 
 @pytest.mark.parametrize("n,chunks,expect", [
@@ -81,6 +108,11 @@ def _worker(rank, world, port, q, mode):
         X, Z, dY = _problem(M, N, K)
         lo, hi = shard_rows(M, world, rank)
         dW_r, db_r = _local_grads(X, Z, dY, lo, hi)
+        if mode == "mlp":
+            q.put((rank, "ok", _mlp_dp_rank(rank, world)))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         if mode == "leave":
             # rank 1 leaves between steps, before its exchange; rank 0's sum must end with an
             # error (peer closed or process-group timeout), not wait for ever
@@ -111,6 +143,40 @@ def _worker(rank, world, port, q, mode):
         dist.destroy_process_group()
     except Exception as exc:  # report to the parent instead of hanging it
         q.put((rank, "error", repr(exc)))
+
+
+_MLP_BATCH, _MLP_LR = 128, 0.05
+
+
+def _mlp_problem():
+    from c3_b200 import mlp
+    params = {k: v.numpy() for k, v in mlp.init_params(11).items()}
+    x, y = mlp.synthetic_batch(12, _MLP_BATCH)
+    return params, x.numpy(), y.numpy()
+
+
+def _mlp_dp_rank(rank, world):
+    """One data-parallel cfg1 step of one rank: oracle gradients on the rank's rows, packed in
+    the step's flat buffer layout, summed by mlp.reduce_gradients over gloo, SGD at
+    mlp.data_parallel_lr."""
+    import torch
+
+    import oracle
+    from c3_b200 import mlp
+    params, x, y = _mlp_problem()
+    lo, hi = mlp.shard_batch(_MLP_BATCH, world, rank)
+    loss, _, g, _ = oracle.mlp_train_step(params, x[lo:hi], y[lo:hi], _MLP_LR)
+    shapes = {k: params[k].shape for k in mlp.PARAM_NAMES}
+    flat = torch.zeros(mlp.flat_numel(shapes))
+    views, loss_slot = mlp.gradient_views(flat, shapes)
+    for k in mlp.PARAM_NAMES:
+        views[k].copy_(torch.from_numpy(g[k]))
+    loss_slot.fill_(loss)
+    mlp.reduce_gradients(flat, world)
+    lr = mlp.data_parallel_lr(_MLP_LR, world)
+    new = {k: oracle.sgd(params[k], views[k].numpy(), lr) for k in mlp.PARAM_NAMES}
+    grads = {k: views[k].numpy() / world for k in mlp.PARAM_NAMES}
+    return float(loss_slot.item()), grads, new
 
 
 def _run(world, mode):
@@ -159,3 +225,31 @@ def test_rank_leaving_is_detected_world2_gloo():
     status, msg = res[0]
     assert status == "ok", msg
     assert msg.startswith("detected")
+
+
+def test_mlp_step_gradient_exchange_world2_gloo():
+    import oracle
+    from c3_b200 import mlp
+    res = _run(2, "mlp")
+    params, x, y = _mlp_problem()
+    loss, _, g, new = oracle.mlp_train_step(params, x, y, _MLP_LR)
+    for rank in range(2):
+        status, out = res[rank]
+        assert status == "ok", f"rank {rank}: {out}"
+        r_loss, r_grads, r_new = out
+        # the mean of the ranks' means is the full-batch mean, up to fp32 rounding
+        assert abs(r_loss - loss) <= 1e-5 * abs(loss), (r_loss, loss)
+        for k in mlp.PARAM_NAMES:
+            ref = float(np.abs(g[k]).max())
+            assert float(np.abs(r_grads[k] - g[k]).max()) <= 1e-5 * max(ref, 1e-30), f"rank {rank} grad {k}"
+            assert float(np.abs(r_new[k] - new[k]).max()) <= 1e-6 * float(np.abs(new[k]).max()) + 1e-9, \
+                f"rank {rank} param {k}"
+    for k in mlp.PARAM_NAMES:  # every rank applies the same update
+        assert np.array_equal(res[0][1][2][k], res[1][1][2][k]), k
+
+
+def test_mlp_shard_batch_needs_equal_shares():
+    from c3_b200 import mlp
+    assert mlp.shard_batch(128, 4, 3) == (96, 128)
+    with pytest.raises(ValueError):
+        mlp.shard_batch(128, 3, 0)

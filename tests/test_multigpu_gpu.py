@@ -1,6 +1,8 @@
 """Data-parallel path on 2 GPUs (child processes, one per GPU): the in-switch all-reduce kernel
-against NCCL's all_reduce on the same buffers, and the row-sharded training step against the
-one-GPU step on the full batch. Skipped when fewer than 2 GPUs are visible."""
+against NCCL's all_reduce on the same buffers, the row-sharded training step against the
+one-GPU step on the full batch, and the data-parallel cfg1 MLP step (eager and CUDA-graph
+replay, one NCCL all-reduce of gradients + loss per step) against the one-GPU full-batch step.
+Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -187,3 +189,86 @@ def test_sharded_step_matches_full_batch(cuda_device):
                 assert v is True, (key, res)
             else:  # db: fp32 sums of two row blocks vs one pass, and summation order
                 assert v <= 1e-5, (key, res)
+
+
+def _mlp_worker(rank, world, port, q):
+    """The data-parallel cfg1 MLP step (c3_b200.mlp.MLPTrainStep with a process group) on its
+    share of the batch against the one-GPU step on the full batch, on this rank's GPU."""
+    try:
+        import datetime
+        import gc
+        import hashlib
+
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        import c3_b200
+        from c3_b200 import mlp
+        B, lr = 128, 0.05
+        params = mlp.init_params(31, dev)
+        full = {k: v.clone() for k, v in params.items()}
+        lo, hi = mlp.shard_batch(B, world, rank)
+        dp = mlp.MLPTrainStep(params, batch=hi - lo, lr=lr, group=dist.group.WORLD)
+        one = mlp.MLPTrainStep(full, batch=B, lr=lr)
+        res = {"loss_err": 0.0, "param_err": 0.0}
+
+        def compare(l_dp, l_one):
+            torch.cuda.synchronize()
+            res["loss_err"] = max(res["loss_err"], abs(float(l_dp) - float(l_one)) / abs(float(l_one)))
+            for k in mlp.PARAM_NAMES:
+                e = float((params[k] - full[k]).abs().max() / full[k].abs().max())
+                res["param_err"] = max(res["param_err"], e)
+
+        for s in range(3):
+            x, y = mlp.synthetic_batch(40 + s, B, dev)
+            l_dp = dp.step(x[lo:hi].contiguous(), y[lo:hi].contiguous()).clone()
+            l_one = one.step(x, y).clone()
+            compare(l_dp.item(), l_one.item())
+        dp.capture()  # the NCCL all-reduce is recorded in the graph with the kernels
+        one.capture()
+        for s in range(3):
+            x, y = mlp.synthetic_batch(50 + s, B, dev)
+            l_dp = dp.replay(x[lo:hi], y[lo:hi]).clone()
+            l_one = one.replay(x, y).clone()
+            compare(l_dp.item(), l_one.item())
+        torch.cuda.synchronize()
+        h = hashlib.sha256()
+        for k in mlp.PARAM_NAMES:
+            h.update(params[k].cpu().numpy().tobytes())
+        res["params_sha"] = h.hexdigest()
+        res["fault"] = c3_b200.fault_status()
+        dp.graph = None  # release the graph that holds NCCL calls before the group goes
+        one.graph = None
+        del dp, one
+        gc.collect()
+        q.put((rank, "ok", res))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc)))
+
+
+def test_data_parallel_mlp_step_matches_full_batch(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mlp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    res = {}
+    for rank, status, r in out:
+        assert status == "ok", f"rank {rank}: {r}"
+        # the sum of two half-batch means against one full-batch mean: fp32 rounding only
+        assert r["loss_err"] <= 1e-5 and r["param_err"] <= 1e-5, r
+        assert r["fault"] == 0
+        res[rank] = r
+    assert res[0]["params_sha"] == res[1]["params_sha"], "ranks hold different parameters"
