@@ -434,6 +434,8 @@ def run_e2e(args, dev, world, rank, comp, X, W, b, dY):
     flops = 3 * 2.0 * M_GLOBAL * N * K
     return {"value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            # per-rank PCIe rates while both directions run: the link bounds this number
+            "h2d_gbs": h2d / (ms * 1e-3) / 1e9, "d2h_gbs": d2h / (ms * 1e-3) / 1e9,
             "path": "c3_b200.linear (C ABI) with pinned host buffers; uploads, compute and downloads "
                     "pipelined across steps on three streams (two device buffer sets)"}
 

@@ -4,7 +4,10 @@
                                 [--variant V] [--dw-dtype bf16|fp32]
 
 cases: gemm-fwd, gemm-dw, gemm-dx, prepass, ew-cfg4, sum-rows, step, attn, mlp-step,
-       mlp-step-graph (the cfg1 training step, eager launches or one CUDA graph)
+       mlp-step-graph (the cfg1 training step, eager launches or one CUDA graph),
+       pcie-h2d, pcie-d2h, pcie-bidir (pinned host <-> device copies of the cfg3 step's
+       inputs X, dY, W, b and results Y, dX, dW, db, one direction or both at once: the link
+       that bounds the end-to-end measurement)
 Prints the CUDA-event time per launch and the algorithmic rate (TFLOP/s or GB/s)."""
 from __future__ import annotations
 
@@ -75,6 +78,31 @@ def _case(args, dev):
         step.x_static.copy_(x)
         step.y_static.copy_(y)
         return (lambda: step.replay()), fl, "TFLOP/s"
+    if args.case.startswith("pcie-"):
+        shapes = [((M, K), torch.bfloat16), ((M, N), torch.bfloat16), ((N, K), torch.bfloat16),
+                  ((N,), torch.float32)]
+        host_in = [torch.ones(s, dtype=t, pin_memory=True) for s, t in shapes]
+        host_out = [torch.empty(s, dtype=t, pin_memory=True) for s, t in shapes]
+        dev_in = [torch.empty(s, dtype=t, device=dev) for s, t in shapes]
+        dev_out = [torch.ones(s, dtype=t, device=dev) for s, t in shapes]
+        nbytes = sum(t.numel() * t.element_size() for t in host_in)
+        up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ups = args.case in ("pcie-h2d", "pcie-bidir")
+        downs = args.case in ("pcie-d2h", "pcie-bidir")
+
+        def copies():
+            cur = torch.cuda.current_stream(dev)
+            active = [(st, pairs) for st, on, pairs in ((up, ups, list(zip(dev_in, host_in))),
+                                                        (down, downs, list(zip(host_out, dev_out)))) if on]
+            for st, _ in active:  # both directions start after the start event, neither waits on the other
+                st.wait_stream(cur)
+            for st, pairs in active:
+                with torch.cuda.stream(st):
+                    for dst, src in pairs:
+                        dst.copy_(src, non_blocking=True)
+            for st, _ in active:
+                cur.wait_stream(st)
+        return copies, nbytes * (2 if args.case == "pcie-bidir" else 1), "GB/s"
     if args.case == "sum-rows":
         x = torch.randn((M, N), generator=g, device=dev)
         out = torch.empty(N, device=dev)
