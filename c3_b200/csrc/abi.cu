@@ -42,6 +42,17 @@ int cuda_status(cudaError_t e, const char* what) {
   return C3CU_ERR_CUDA;
 }
 
+int set_max_dynamic_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, const char* what) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), what);
+  if (rc != C3CU_OK) return rc;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t{1} << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return C3CU_OK;
+  rc = cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (rc == C3CU_OK && bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+  return rc;
+}
+
 int sm_count() {
   static std::mutex mu;
   static std::vector<int> cache;

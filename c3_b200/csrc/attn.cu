@@ -430,14 +430,10 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
   p.O = static_cast<__nv_bfloat16*>(O);
   p.lse = LSE;
   if (attn::g_attn_variant == 1) {
-    static bool attr = false;
-    if (!attr) {
-      rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            attn::SMEM_BYTES),
-                       "flash_attn_fwd: set shared memory");
-      if (rc != C3CU_OK) return rc;
-      attr = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd_kernel), attn::SMEM_BYTES,
+                              smem_set, "flash_attn_fwd: set shared memory");
+    if (rc != C3CU_OK) return rc;
     const int64_t grid = static_cast<int64_t>(p.BH) * p.q_tiles;
     if (grid > INT32_MAX) {
       set_error("flash_attn_fwd: grid too large");
@@ -457,24 +453,21 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
     CUtensorMap tk64, tv64;
     if ((rc = attn::encode_bhsd(&tk64, K, B * H, S, 64)) != C3CU_OK) return rc;
     if ((rc = attn::encode_bhsd(&tv64, V, B * H, S, 64)) != C3CU_OK) return rc;
-    rc = cuda_status(cudaFuncSetAttribute(attn::flash_fwd3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          attn::SMEM_BYTES3),
-                     "flash_attn_fwd: set shared memory");
+    static std::atomic<uint64_t> smem_set3{0};
+    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd3_kernel), attn::SMEM_BYTES3,
+                              smem_set3, "flash_attn_fwd: set shared memory");
     if (rc != C3CU_OK) return rc;
     attn::flash_fwd3_kernel<<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
                               static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
     return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
   }
-  auto go = [&](auto kern) -> int {
-    int r = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             attn::SMEM_BYTES2),
-                        "flash_attn_fwd: set shared memory");
-    if (r != C3CU_OK) return r;
-    kern<<<static_cast<unsigned>(grid), attn::kThreads2, attn::SMEM_BYTES2,
-           static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-    return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
-  };
-  return go(attn::flash_fwd2_kernel);
+  static std::atomic<uint64_t> smem_set2{0};
+  rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd2_kernel), attn::SMEM_BYTES2,
+                            smem_set2, "flash_attn_fwd: set shared memory");
+  if (rc != C3CU_OK) return rc;
+  attn::flash_fwd2_kernel<<<static_cast<unsigned>(grid), attn::kThreads2, attn::SMEM_BYTES2,
+                            static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
 }
 
 extern "C" int c3cu_set_attn_variant(int variant) {

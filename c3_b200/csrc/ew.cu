@@ -219,8 +219,12 @@ int ticket_pool(cudaStream_t st, unsigned int** out) {
   void* p = nullptr;
   rc = cuda_status(cudaMalloc(&p, kPoolStrips * 4), "column sum: ticket array");
   if (rc != C3CU_OK) return rc;
-  rc = cuda_status(cudaMemset(p, 0, kPoolStrips * 4), "column sum: clear ticket array");
-  if (rc != C3CU_OK) return rc;
+  // cleared on the stream that will use it (ordered before its first launch on any stream kind)
+  rc = cuda_status(cudaMemsetAsync(p, 0, kPoolStrips * 4, st), "column sum: clear ticket array");
+  if (rc != C3CU_OK) {
+    cudaFree(p);
+    return rc;
+  }
   pool.push_back({{dev, st}, p});
   *out = static_cast<unsigned int*>(p);
   return C3CU_OK;

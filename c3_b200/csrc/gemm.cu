@@ -41,10 +41,11 @@ std::atomic<int> g_variant{0};
 // Co-resident clusters of two CTAs for a kernel (cached per device and kernel).
 template <class Kern>
 int max_pair_clusters(Kern kern, uint32_t smem_bytes, int threads) {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cached[dev] > 0) return cached[dev];
+  const int have = cached[dev].load(std::memory_order_relaxed);
+  if (have > 0) return have;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 74, 1, 1);
   cfg.blockDim = dim3(threads, 1, 1);
@@ -61,7 +62,7 @@ int max_pair_clusters(Kern kern, uint32_t smem_bytes, int threads) {
     cudaGetLastError();
     return 0;
   }
-  cached[dev] = n;
+  cached[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -88,8 +89,14 @@ int split_workspace(cudaStream_t stream, float** partial, uint32_t** tickets, ui
       ws = nullptr;
       return rc;
     }
-    rc = cuda_status(cudaMemset(ws, 0, kSplitWsBytes), "gemm2: clear split-K workspace");
-    if (rc != C3CU_OK) return rc;
+    // cleared on the stream that will use it, so the clear precedes its first launch even on
+    // a stream that does not synchronise with the legacy default stream
+    rc = cuda_status(cudaMemsetAsync(ws, 0, kSplitWsBytes, stream), "gemm2: clear split-K workspace");
+    if (rc != C3CU_OK) {
+      cudaFree(ws);
+      ws = nullptr;
+      return rc;
+    }
   }
   *partial = static_cast<float*>(ws);
   *tickets = reinterpret_cast<uint32_t*>(*partial + kSplitPartialFloats);
@@ -115,14 +122,10 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   if (rc != C3CU_OK) return rc;
 
   auto kern = gemm2::gemm2_kernel<A_MN, B_MN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          gemm2::SMEM_BYTES),
-                     "gemm2: set max dynamic shared memory");
-    if (rc != C3CU_OK) return rc;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};  // per instantiation, one bit per device
+  rc = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), gemm2::SMEM_BYTES, smem_set,
+                            "gemm2: set max dynamic shared memory");
+  if (rc != C3CU_OK) return rc;
   const int tiles = ((p.M + gemm2::TM - 1) / gemm2::TM) * ((p.N + gemm2::TN - 1) / gemm2::TN);
   int clusters = max_pair_clusters(kern, gemm2::SMEM_BYTES, gemm2::kThreads);
   if (clusters <= 0) clusters = sm_count() / 2;
@@ -179,14 +182,10 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   if (rc != C3CU_OK) return rc;
 
   auto kern = gemm::gemm_kernel<A_MN, B_MN, EPI>;
-  static bool attr_set = false;  // per instantiation; idempotent, so a race is harmless
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          gemm::SMEM_BYTES),
-                     "gemm: set max dynamic shared memory");
-    if (rc != C3CU_OK) return rc;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};  // per instantiation, one bit per device
+  rc = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), gemm::SMEM_BYTES, smem_set,
+                            "gemm: set max dynamic shared memory");
+  if (rc != C3CU_OK) return rc;
   const int tiles = ((p.M + gemm::BM - 1) / gemm::BM) * ((p.N + gemm::BN - 1) / gemm::BN);
   int sms = sm_count();
   const int cap = g_max_ctas.load(std::memory_order_relaxed);

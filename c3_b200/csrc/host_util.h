@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -20,6 +21,11 @@ void set_error(const char* fmt, ...);
 
 // Returns C3CU_ERR_CUDA (and records the message) when `e` is an error.
 int cuda_status(cudaError_t e, const char* what);
+
+// Raises the dynamic shared memory limit of `kernel` to `bytes` on the current device, once per
+// device: cudaFuncSetAttribute applies to the current device only. `done` is the caller's
+// per-kernel bitmask of devices already set (devices 64 and above are set on every call).
+int set_max_dynamic_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, const char* what);
 
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
