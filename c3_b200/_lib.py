@@ -5,6 +5,7 @@ the current device is not an sm_100 part, every entry point raises C3CUError."""
 from __future__ import annotations
 
 import ctypes
+import functools
 import re
 import threading
 from pathlib import Path
@@ -125,3 +126,33 @@ def fault_status() -> int:
     rc = load().c3cu_fault_status(ctypes.byref(code))
     check(rc, "c3cu_fault_status")
     return code.value
+
+
+def _cuda_devices(values, found: set) -> None:
+    import torch
+    for v in values:
+        if isinstance(v, torch.Tensor):
+            if v.is_cuda:
+                found.add(v.device.index)
+        elif isinstance(v, (list, tuple)):
+            _cuda_devices(v, found)
+
+
+def on_tensor_device(fn):
+    """Runs a wrapper of the C ABI on the device of its CUDA tensor arguments. The library
+    launches on the current device with that device's stream, so the call is made with the
+    tensors' device current (as torch ops do). Tensors on different devices are refused before
+    any launch: a kernel reading another GPU's memory without peer access would fault."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        import torch
+        found: set = set()
+        _cuda_devices(args, found)
+        _cuda_devices(kwargs.values(), found)
+        if not found:
+            return fn(*args, **kwargs)
+        if len(found) > 1:
+            raise C3CUError(-1, fn.__name__, f"tensors on different devices: cuda:{sorted(found)}")
+        with torch.cuda.device(found.pop()):
+            return fn(*args, **kwargs)
+    return wrapper

@@ -10,6 +10,7 @@ from . import _lib
 from .linear import _p, _stream
 
 
+@_lib.on_tensor_device
 def flash_attn_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = True,
                    scale: float | None = None, out: torch.Tensor | None = None,
                    lse: torch.Tensor | None = None):

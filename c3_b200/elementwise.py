@@ -13,6 +13,7 @@ from .linear import _p, _stream, workspace
 ADD, SUB, MUL, DIV, DIV_NANZ, NEG, RELU, EXP, LOG, SIGMOID, TANH, TANH_EXP, GT, CONST, MOV = range(1, 16)
 
 
+@_lib.on_tensor_device
 def chain_cfg4(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, out: torch.Tensor | None = None):
     """out = relu((A + B) * C - A) / (1 + exp(-B)), fp32, one pass over HBM."""
     for t, n in ((A, "A"), (B, "B"), (C, "C")):
@@ -27,6 +28,7 @@ def chain_cfg4(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, out: torch.Ten
     return out
 
 
+@_lib.on_tensor_device
 def program(inputs: list[torch.Tensor], code: list[tuple[int, int, int, int]], constants: list[float],
             out_reg: int, n: int, out: torch.Tensor | None = None):
     """Runs a register-machine chain: registers 0..len(inputs)-1 hold inputs[i][idx % numel]."""
@@ -46,6 +48,7 @@ def program(inputs: list[torch.Tensor], code: list[tuple[int, int, int, int]], c
     return out
 
 
+@_lib.on_tensor_device
 def sum_rows(x: torch.Tensor, out: torch.Tensor | None = None):
     """Column sums of an fp32 matrix (SumReduce axis 0), deterministic order."""
     M, N = x.shape
@@ -62,6 +65,7 @@ def sum_rows(x: torch.Tensor, out: torch.Tensor | None = None):
 BW_OPS = {"ReLU": 1, "Sigmoid": 2, "Tanh": 3, "Neg": 4, "Exp": 5, "Log": 6}
 
 
+@_lib.on_tensor_device
 def backward_chain(types: list[str], grad: torch.Tensor, xs: list[torch.Tensor | None],
                    outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
     """Fused backward of a chain of unary elementwise nodes (types[0] most downstream):

@@ -53,6 +53,7 @@ def mask_words(n: int) -> int:
     return (n + 31) // 32
 
 
+@_lib.on_tensor_device
 def forward(X: torch.Tensor, W: torch.Tensor, b: torch.Tensor, w_layout: str = "nk",
             Y: torch.Tensor | None = None, mask: torch.Tensor | None = None):
     """Y = max(X W^T + b, 0) (or X B + b), bf16 out, plus the bit-packed ReLU mask
@@ -77,6 +78,7 @@ def forward(X: torch.Tensor, W: torch.Tensor, b: torch.Tensor, w_layout: str = "
     return Y, mask
 
 
+@_lib.on_tensor_device
 def relu_mask_db(dY: torch.Tensor, mask: torch.Tensor, dZ: torch.Tensor | None = None,
                  db: torch.Tensor | None = None):
     """dZ = float(mask) * dY (bf16, exact) and db = column sums of dZ (fp32)."""
@@ -96,6 +98,7 @@ def relu_mask_db(dY: torch.Tensor, mask: torch.Tensor, dZ: torch.Tensor | None =
     return dZ, db
 
 
+@_lib.on_tensor_device
 def grad_input(dZ: torch.Tensor, W: torch.Tensor, w_layout: str = "nk", dX: torch.Tensor | None = None):
     lay = _layout(w_layout)
     _require(dZ, "dZ", torch.bfloat16, 2)
@@ -109,6 +112,7 @@ def grad_input(dZ: torch.Tensor, W: torch.Tensor, w_layout: str = "nk", dX: torc
     return dX
 
 
+@_lib.on_tensor_device
 def grad_weight(dZ: torch.Tensor, X: torch.Tensor, w_layout: str = "nk", dW: torch.Tensor | None = None,
                 out_dtype: torch.dtype = torch.float32):
     """dW = dZ^T X ([N, K], "nk") or X^T dZ ([K, N], "kn"), fp32 or bf16 (fp32 accumulation)."""
@@ -130,6 +134,7 @@ def grad_weight(dZ: torch.Tensor, X: torch.Tensor, w_layout: str = "nk", dW: tor
     return dW
 
 
+@_lib.on_tensor_device
 def backward(dY: torch.Tensor, mask: torch.Tensor, X: torch.Tensor, W: torch.Tensor,
              w_layout: str = "nk"):
     """Captured backward of the region: returns (dX bf16, dW fp32, db fp32)."""
@@ -139,6 +144,7 @@ def backward(dY: torch.Tensor, mask: torch.Tensor, X: torch.Tensor, W: torch.Ten
     return dX, dW, db
 
 
+@_lib.on_tensor_device
 def gemm(A: torch.Tensor, B: torch.Tensor, a_mn: bool, b_mn: bool, epilogue: int,
          out: torch.Tensor, bias: torch.Tensor | None = None, mask: torch.Tensor | None = None,
          M: int | None = None, N: int | None = None, K: int | None = None):

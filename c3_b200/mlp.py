@@ -178,7 +178,14 @@ class MLPTrainStep:
 
     # ------------------------------------------------------------------ the step
     def step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-        """Forward, loss, backward and SGD update for one batch; returns the device scalar loss."""
+        """Forward, loss, backward and SGD update for one batch; returns the device scalar loss.
+        Runs on the parameters' device whichever device is current."""
+        with torch.cuda.device(self.device):
+            return self._step(x, y)
+
+    def _step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        if x.device != self.device or y.device != self.device:
+            raise _lib.C3CUError(-1, "MLPTrainStep.step", f"x and y must be on {self.device}")
         if x.shape != (self.B, LAYERS[0]) or x.dtype != torch.float32 or not x.is_contiguous():
             raise _lib.C3CUError(-1, "MLPTrainStep.step", f"x must be contiguous fp32 [{self.B}, {LAYERS[0]}]")
         if y.shape != (self.B,) or y.dtype != torch.int32:

@@ -33,3 +33,16 @@ def test_workspace_size_queries_are_pure_host():
     assert lib.c3cu_relu_mask_db_workspace(16384, 4096) >= 32 * 4096 * 4
     assert lib.c3cu_relu_mask_db_workspace(0, 10) > 0
     assert lib.c3cu_sum_rows_f32_workspace(5, 5) > 0
+
+
+def test_device_wrapper_passes_host_calls_through():
+    """on_tensor_device leaves calls without CUDA tensors alone (no device is touched)."""
+    import torch
+    from c3_b200 import _lib
+
+    @_lib.on_tensor_device
+    def f(a, b=None, xs=()):
+        return a.sum() + (0 if b is None else b.sum()) + sum(x.sum() for x in xs)
+
+    t = torch.ones(3)
+    assert float(f(t, b=t, xs=[t, t])) == 12.0

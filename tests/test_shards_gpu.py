@@ -60,3 +60,39 @@ def test_attention_head_shards_reassemble(cuda_device, world):
         torch.cuda.synchronize()
         assert torch.equal(Os, flat(O)[:, lo:hi]), f"rank {r} of {world}: O"
         assert torch.equal(Ls, L.view(1, Bt * H, S)[:, lo:hi]), f"rank {r} of {world}: LSE"
+
+
+def test_one_process_on_two_devices(cuda_device):
+    """A host that drives two GPUs from one process, with cuda:0 current throughout: the
+    wrappers run each call on its tensors' device, every kernel's launch setup (shared memory
+    limits, workspaces, tensor maps) is per device, and both devices give the same bits for the
+    same inputs. Tensors on different devices are refused before any launch."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from c3_b200 import _lib, mlp
+    torch.cuda.set_device(0)
+    outs = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        g = torch.Generator(device=dev).manual_seed(9)
+        X = torch.randn((1024, 768), generator=g, device=dev).to(torch.bfloat16)
+        W = (torch.randn((512, 768), generator=g, device=dev) * 0.05).to(torch.bfloat16)
+        b = torch.randn((512,), generator=g, device=dev) * 0.05
+        dY = (torch.randn((1024, 512), generator=g, device=dev) * 1e-2).to(torch.bfloat16)
+        Y, mask = linear.forward(X, W, b, "nk")
+        dZ, db = linear.relu_mask_db(dY, mask)
+        dW = linear.grad_weight(dZ, X, "nk")
+        Q, K, V = (torch.randn((1, 2, 256, 128), generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(3))
+        O, L = flash_attn_fwd(Q, K, V, causal=True)
+        params = mlp.init_params(3, dev)
+        x, y = mlp.synthetic_batch(4, 128, dev)
+        loss = mlp.MLPTrainStep(params, batch=128).step(x, y)
+        torch.cuda.synchronize(dev)
+        assert torch.cuda.current_device() == 0
+        outs.append([t.cpu() for t in (Y, mask, dZ, db, dW, O, L, loss, params["W1"])])
+        if d == 1:
+            with pytest.raises(_lib.C3CUError):
+                linear.forward(X, W.to("cuda:0"), b, "nk")
+    for name, a, c in zip(("Y", "mask", "dZ", "db", "dW", "O", "LSE", "loss", "W1"), *outs):
+        assert torch.equal(a, c), name
