@@ -46,3 +46,68 @@ def test_device_wrapper_passes_host_calls_through():
 
     t = torch.ones(3)
     assert float(f(t, b=t, xs=[t, t])) == 12.0
+
+
+def _header_prototypes():
+    """{name: (return type, [parameter types])} of every function declared in include/*.h."""
+    import re
+    from pathlib import Path
+    protos = {}
+    for h in sorted((Path(_lib.PKG).parent / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        text = re.sub(r"#[^\n]*", "", text)
+        for m in re.finditer(r"([A-Za-z_][\w\s\*]*?)\b(c3cu_\w+)\s*\(([^)]*)\)\s*;", text):
+            ret, name, params = m.group(1).strip(), m.group(2), m.group(3).strip()
+            plist = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+            types = [re.sub(r"\s*\b\w+$", "", p) if not p.endswith("*") else p for p in plist]
+            protos[name] = (ret, types)
+    return protos
+
+
+def _kind_of_c(t: str) -> str:
+    t = t.replace("const", "").strip()
+    if "*" in t or t in ("c3cu_stream_t",):
+        return "ptr"
+    if t == "float":
+        return "f32"
+    if t == "double":
+        return "f64"
+    if t in ("int", "int32_t", "uint32_t", "unsigned", "unsigned int"):
+        return "i32"
+    if t in ("int64_t", "size_t", "uint64_t", "long long"):
+        return "i64"
+    return "?" + t
+
+
+def _kind_of_ctypes(t) -> str:
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(t, type) and issubclass(t, ctypes._Pointer)):
+        return "ptr"
+    if t is ctypes.c_float:
+        return "f32"
+    if t is ctypes.c_double:
+        return "f64"
+    if t in (ctypes.c_int, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint):
+        return "i32"
+    if t in (ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_longlong):
+        return "i64"
+    return "?" + repr(t)
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every signature the Python wrappers declare agrees with include/c3cu.h in arity and in
+    the kind of each argument and of the result: a wrong one would pass a stream or a size in
+    the wrong slot without any error."""
+    protos = _header_prototypes()
+    assert "c3cu_gemm_bf16" in protos and len(protos["c3cu_gemm_bf16"][1]) == 16
+    bad = []
+    for name, (args, res) in _lib._SIGNATURES.items():
+        assert name in protos, f"{name} has a ctypes signature but no declaration"
+        ret, ptypes = protos[name]
+        want = [_kind_of_c(t) for t in ptypes]
+        got = [_kind_of_ctypes(t) for t in args]
+        if want != got:
+            bad.append(f"{name}: header {want} vs ctypes {got}")
+        if _kind_of_c(ret) != _kind_of_ctypes(res):
+            bad.append(f"{name}: returns {ret} in the header, {res} in ctypes")
+    assert not bad, "\n".join(bad)
