@@ -24,6 +24,16 @@ namespace ew {
 constexpr int kColsPerWarp = 256;   // 32 lanes x 8 columns
 constexpr int kWarps = 8;
 constexpr int kRowsPerBlock = 512;  // rows one block reduces before the cross-block pass
+#ifndef C3CU_COLSUM_PREFETCH
+#define C3CU_COLSUM_PREFETCH 1
+#endif
+constexpr bool kColsumPrefetch = C3CU_COLSUM_PREFETCH != 0;
+
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte-aligned global address; no data is
+// returned and no register is held.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // ------------------------------------------------------------------ column sums
 // One block covers a strip of 256 columns and up to 512 rows. Each thread owns 8 adjacent
@@ -135,10 +145,26 @@ __global__ void __launch_bounds__(kWarps * 32)
   if (col < N) {
     const bool vec = vec_ok && (col + 8 <= N);
     int r = row0 + warp;
+    // Rows of the next batch are prefetched into L2 (one bulk prefetch of the warp's row segment,
+    // issued by lane 0) while this batch is consumed: twice the DRAM requests in flight per
+    // warp without more registers. Only whole 16-byte-aligned segments of valid rows.
+    const int seg_cols = min(kColsPerWarp, N - strip * kColsPerWarp);
+    const uint32_t seg_bytes = static_cast<uint32_t>(seg_cols) * (MASKED ? 2u : 4u);
+    const bool prefetch = kColsumPrefetch && vec_ok && lane == 0 && (seg_bytes & 15u) == 0u;
+    const char* seg0 = static_cast<const char*>(in) +
+                       static_cast<int64_t>(strip) * kColsPerWarp * (MASKED ? 2 : 4);
+    const int64_t row_bytes = static_cast<int64_t>(N) * (MASKED ? 2 : 4);
     for (; r + 3 * kWarps < row1; r += 4 * kWarps) {
       uint32_t raw[4][8], bits[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) colsum_load<MASKED>(in, mask, r + u * kWarps, col, N, ldm, vec, raw[u], bits[u]);
+      if (prefetch) {
+#pragma unroll
+        for (int u = 4; u < 8; ++u) {
+          const int rn = r + u * kWarps;
+          if (rn < row1) prefetch_l2_bulk(seg0 + rn * row_bytes, seg_bytes);
+        }
+      }
 #pragma unroll
       for (int u = 0; u < 4; ++u) colsum_consume<MASKED>(dz, r + u * kWarps, col, N, vec, raw[u], bits[u], acc);
     }
