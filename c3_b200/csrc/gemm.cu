@@ -131,33 +131,18 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   if (clusters <= 0) clusters = sm_count() / 2;
   const int cap = g_max_ctas.load(std::memory_order_relaxed);
   if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
-  // Split-K tail (automatic variant only, K at least 64 blocks): when the last wave would
-  // leave at least half of the clusters idle, its tiles run as two K halves on two clusters
-  // each. With shorter K the fp32 partial exchange costs about as much as a half's main loop
-  // (measured: dW with K = 2048 ran 5% slower split).
-  // (A stream-K split of the last waves balanced the clusters exactly but ran slower: the
-  // shorter pieces and their fix-ups left the tensor pipe waiting on the epilogue.)
-  Params q = p;
-  q.sk_mode = 0;
-  q.sk_first = 0;
+  // Split-K tail (gemm2::plan_split; measured: dW with K = 2048 ran 5% slower split, hence the
+  // 64-block minimum). A stream-K split of the last waves balanced the clusters exactly but ran
+  // slower: the shorter pieces and their fix-ups left the tensor pipe waiting on the epilogue.
   const int k_blocks = (p.K + gemm2::BK - 1) / gemm2::BK;
-  if (variant == 0 && k_blocks >= 64) {
-    const int tail = tiles % clusters;
-    if (tail > 0 && 2 * tail <= clusters) {
-      q.sk_mode = 1;
-      q.sk_first = tiles - tail;
-      if (tiles < clusters) clusters = 2 * tiles;
-    }
-  }
-  if (q.sk_mode == 0 && tiles < clusters) clusters = tiles;
+  const gemm2::SplitPlan plan = gemm2::plan_split(tiles, clusters, k_blocks, variant, kSplitMax);
+  Params q = p;
+  q.sk_mode = plan.sk_mode;
+  q.sk_first = plan.sk_first;
+  clusters = plan.clusters;
   if (q.sk_mode != 0) {
-    if (clusters > kSplitMax) {
-      q.sk_mode = 0;  // more boundary slots than the workspace holds: whole tiles
-      if (tiles < clusters) clusters = tiles;
-    } else {
-      rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
-      if (rc != C3CU_OK) return rc;
-    }
+    rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
+    if (rc != C3CU_OK) return rc;
   }
   kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, q);
   return cuda_status(cudaGetLastError(), "gemm2: launch");

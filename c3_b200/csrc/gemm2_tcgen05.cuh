@@ -22,6 +22,7 @@
 // Loads use no cluster multicast: every CTA reads its own operands from global memory.
 #pragma once
 
+#include "gemm2_schedule.h"
 #include "gemm_tcgen05.cuh"
 
 namespace c3cu {
@@ -77,29 +78,6 @@ __device__ __forceinline__ void settle_inflight_copies() {
 // One unit of a cluster's work: an output tile and the K blocks [kb0, kb1) to accumulate.
 // split >= 0 marks a tile that two clusters share as two K halves (the index of its fp32
 // partial slot); the two halves meet through a ticket in the epilogue.
-struct Item {
-  int tile, kb0, kb1, split;
-};
-
-// Work of cluster `c` of `C`: the tiles c, c + C, ... below sk_first (whole waves; all
-// tiles when sk_mode is 0), then, with sk_mode 1, K half (c & 1) of tail tile
-// sk_first + (c >> 1) for c < 2 * (num_tiles - sk_first). The host uses the tail split when
-// the last wave would leave at least half of the clusters idle.
-__device__ __forceinline__ bool work_item(int i, int c, int C, int num_tiles, int sk_mode,
-                                          int sk_first, int k_blocks, Item& it) {
-  const int t_dp = sk_mode == 1 ? sk_first : num_tiles;
-  const int n_dp = t_dp > c ? (t_dp - c + C - 1) / C : 0;
-  if (i < n_dp) {
-    it = Item{c + i * C, 0, k_blocks, -1};
-    return true;
-  }
-  if (sk_mode != 1 || i != n_dp || c >= 2 * (num_tiles - t_dp)) return false;
-  const int kmid = k_blocks / 2;
-  const bool hi = (c & 1) != 0;
-  it = Item{t_dp + (c >> 1), hi ? kmid : 0, hi ? k_blocks : kmid, c >> 1};
-  return true;
-}
-
 // Bounded acquire-wait for a split partner's "partial published" word.
 __device__ __forceinline__ bool wait_ready(const uint32_t* flag) {
   const uint64_t t0 = globaltimer_ns();

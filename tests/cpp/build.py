@@ -18,12 +18,13 @@ def build() -> Path:
     lib = lib_build.build()
     olib = oracle.build()
     src = HERE / "test_host_api.cpp"
-    headers = list((ROOT / "c3_b200" / "csrc" / "host").rglob("*.h")) + [ROOT / "include" / "c3cu.h"]
+    headers = list((ROOT / "c3_b200" / "csrc" / "host").rglob("*.h")) + [ROOT / "include" / "c3cu.h",
+                                                                           ROOT / "c3_b200" / "csrc" / "gemm2_schedule.h"]
     if OUT.exists() and all(OUT.stat().st_mtime >= p.stat().st_mtime for p in [src, lib, olib] + headers):
         return OUT
     OUT.parent.mkdir(exist_ok=True)
     cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-pthread", str(src), "-o", str(OUT),
-           f"-I{ROOT / 'c3_b200' / 'csrc' / 'host'}", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
+           f"-I{ROOT / 'c3_b200' / 'csrc' / 'host'}", f"-I{ROOT / 'c3_b200' / 'csrc'}", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
            f"-L{lib.parent}", "-lc3cu", f"-Wl,-rpath,{lib.parent}", f"-L{olib.parent}", "-loracle",
            f"-Wl,-rpath,{olib.parent}"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <array>
 #include <cstring>
 #include <functional>
 #include <random>
@@ -27,6 +28,7 @@
 #include "C3/RegionFusion.h"
 #include "C3/RollingHash.h"
 #include "c3cu.h"
+#include "gemm2_schedule.h"
 
 extern "C" {
 void c3o_region_fwd(const float* X, const float* B, const float* b, size_t b_numel, float* out, float* z,
@@ -127,6 +129,70 @@ static Graph regionGraph(size_t M, size_t K, size_t N) {
 }
 
 // ============================================================================ CPU
+// The CTA-pair GEMM's work schedule (the launcher's split plan and the kernel's per-cluster
+// items, c3_b200/csrc/gemm2_schedule.h) over every cluster count a B200 launch can have
+// (1..74, including SM caps) and a sweep of tile counts and K depths: every output tile's K
+// range is computed exactly once, either whole or as two non-empty halves on the two clusters
+// that share its split slot; no launched cluster is idle; the slot fits the workspace.
+TEST(gemm2_schedule_covers_every_tile_once, false) {
+  using c3cu::gemm2::Item;
+  const int split_slots = 80;
+  std::vector<int> tile_counts;
+  for (int t = 1; t <= 400; ++t) tile_counts.push_back(t);
+  for (int t : {512, 1024, 1152, 4096}) tile_counts.push_back(t);
+  std::vector<std::array<Item, 3>> seen;
+  std::vector<int> nseen;
+  long configs = 0, bad = 0;
+  for (int variant : {0, 2})
+    for (int kb : {1, 2, 63, 64, 65, 127, 128})
+      for (int maxc = 1; maxc <= 74; ++maxc)
+        for (int tiles : tile_counts) {
+          ++configs;
+          const auto plan = c3cu::gemm2::plan_split(tiles, maxc, kb, variant, split_slots);
+          bool ok = plan.clusters >= 1 && plan.clusters <= maxc && (plan.sk_mode == 0 || plan.sk_mode == 1);
+          if (plan.sk_mode == 1) ok = ok && variant == 0 && kb >= 64 && plan.sk_first >= 0 && plan.sk_first < tiles;
+          seen.assign(tiles, {});
+          nseen.assign(tiles, 0);
+          for (int c = 0; ok && c < plan.clusters; ++c) {
+            Item it{};
+            int i = 0;
+            for (; c3cu::gemm2::work_item(i, c, plan.clusters, tiles, plan.sk_mode, plan.sk_first, kb, it); ++i) {
+              if (it.tile < 0 || it.tile >= tiles || nseen[it.tile] >= 2) { ok = false; break; }
+              Item rec = it;
+              rec.split = it.split < 0 ? -1 : (it.split << 8) | c;  // remember the cluster too
+              seen[it.tile][nseen[it.tile]++] = rec;
+            }
+            if (i == 0) ok = false;  // a launched cluster with no work
+          }
+          for (int t = 0; ok && t < tiles; ++t) {
+            if (nseen[t] == 1) {
+              const Item& a = seen[t][0];
+              ok = a.kb0 == 0 && a.kb1 == kb && a.split == -1;
+            } else if (nseen[t] == 2) {
+              Item a = seen[t][0], b = seen[t][1];
+              if (a.kb0 > b.kb0) std::swap(a, b);
+              const int slot = a.split >> 8;
+              ok = plan.sk_mode == 1 && a.split >= 0 && b.split >= 0 && slot == (b.split >> 8) &&
+                   slot == t - plan.sk_first && slot < split_slots && a.kb0 == 0 && a.kb1 == b.kb0 &&
+                   b.kb1 == kb && a.kb1 > 0 && b.kb0 < kb && (a.split & 0xff) == 2 * slot &&
+                   (b.split & 0xff) == 2 * slot + 1;
+            } else {
+              ok = false;
+            }
+          }
+          if (!ok && ++bad <= 5)
+            std::fprintf(stderr, "  schedule wrong: variant %d, k_blocks %d, clusters %d, tiles %d\n", variant,
+                         kb, maxc, tiles);
+        }
+  CHECK(bad == 0);
+  CHECK(configs > 400000);
+  // the cfg3 dW GEMM: 256 tiles on 74 pairs splits the 34 tail tiles over 68 clusters
+  const auto dw = c3cu::gemm2::plan_split(256, 74, 64, 0, split_slots);
+  CHECK(dw.sk_mode == 1 && dw.sk_first == 222 && dw.clusters == 74);
+  // K = 2048 (32 blocks) never splits
+  CHECK(c3cu::gemm2::plan_split(256, 74, 32, 0, split_slots).sk_mode == 0);
+}
+
 TEST(rolling_hash_known_answers, false) {
   // ((13*131)+2)*131+29 for {MatMul, Add, ReLU} (codes MatMul 13, Add 2, ReLU 29)
   CHECK(RollingHash::hashSequence({op::MatMul, op::Add, op::ReLU}) == 223384ull);
