@@ -153,6 +153,9 @@ def on_tensor_device(fn):
             return fn(*args, **kwargs)
         if len(found) > 1:
             raise C3CUError(-1, fn.__name__, f"tensors on different devices: cuda:{sorted(found)}")
-        with torch.cuda.device(found.pop()):
+        idx = found.pop()
+        if idx == torch.cuda.current_device():  # the common case: no device switch
+            return fn(*args, **kwargs)
+        with torch.cuda.device(idx):
             return fn(*args, **kwargs)
     return wrapper
