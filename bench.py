@@ -121,8 +121,7 @@ def run_reference(args):
     import oracle
     threads = oracle.default_threads()
     rng = np.random.default_rng(0)
-    bf = lambda a: a.astype(np.float32)  # values are drawn on the bf16 grid below
-    def bf16_grid(a):
+    def bf16_grid(a):  # round to nearest even on the bf16 grid, kept as fp32
         u = a.astype(np.float32).view(np.uint32)
         return ((u + 0x7fff + ((u >> 16) & 1)) & 0xffff0000).view(np.float32)
     W = bf16_grid(rng.standard_normal((N_DIM, K_DIM), dtype=np.float32) * 0.02)
