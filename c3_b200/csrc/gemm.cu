@@ -19,7 +19,8 @@ using gemm::Params;
 
 // Upper bound on the persistent GEMM's CTAs (0 = one per SM). Lowering it leaves SMs free
 // for a collective that runs concurrently (e.g. an all-reduce overlapped with the dX GEMM).
-std::atomic<int> g_max_ctas{0};
+// Per host thread: a cap set around one launch never reaches GEMMs other threads launch.
+thread_local int g_max_ctas = 0;
 
 // Per-shape variants chosen by a tuner (c3cu_gemm_tune_set); they take precedence over
 // g_variant for an exact (M, N, K, majors, epilogue) match.
@@ -129,7 +130,7 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   const int tiles = ((p.M + gemm2::TM - 1) / gemm2::TM) * ((p.N + gemm2::TN - 1) / gemm2::TN);
   int clusters = max_pair_clusters(kern, gemm2::SMEM_BYTES, gemm2::kThreads);
   if (clusters <= 0) clusters = sm_count() / 2;
-  const int cap = g_max_ctas.load(std::memory_order_relaxed);
+  const int cap = g_max_ctas;
   if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
   // Split-K tail (gemm2::plan_split; measured: dW with K = 2048 ran 5% slower split, hence the
   // 64-block minimum). A stream-K split of the last waves balanced the clusters exactly but ran
@@ -173,7 +174,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   if (rc != C3CU_OK) return rc;
   const int tiles = ((p.M + gemm::BM - 1) / gemm::BM) * ((p.N + gemm::BN - 1) / gemm::BN);
   int sms = sm_count();
-  const int cap = g_max_ctas.load(std::memory_order_relaxed);
+  const int cap = g_max_ctas;
   if (cap > 0 && cap < sms) sms = cap;
   const int grid = tiles < sms ? tiles : sms;
   kern<<<grid, gemm::kThreads, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
@@ -278,7 +279,7 @@ int c3cu_set_gemm_max_ctas(int max_ctas) {
     c3cu::set_error("set_gemm_max_ctas: negative limit");
     return C3CU_ERR_INVALID;
   }
-  c3cu::g_max_ctas.store(max_ctas, std::memory_order_relaxed);
+  c3cu::g_max_ctas = max_ctas;
   return C3CU_OK;
 }
 

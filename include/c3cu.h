@@ -123,8 +123,9 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    void* out, int64_t ldo, int epilogue, const float* bias, uint32_t* mask,
                    int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream);
 
-/* Library-wide cap on the CTAs of the persistent tensor-core GEMMs (0 = one per SM, the
- * default). A host that overlaps a collective with a GEMM lowers it to leave SMs free. */
+/* Cap on the CTAs of the persistent tensor-core GEMMs that the CALLING THREAD launches from now
+ * on (0 = one per SM, the default). A host that overlaps a collective with a GEMM lowers it
+ * around that launch to leave SMs free; GEMMs launched by other threads are not affected. */
 int c3cu_set_gemm_max_ctas(int max_ctas);
 /* GEMM kernel variant for the calls that follow (process-wide): 0 = automatic (the CTA-pair
  * kernel, 256 x 256 tiles on two SMs with cta_group::2, whenever M > 128, else the single-CTA
