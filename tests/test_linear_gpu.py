@@ -215,6 +215,50 @@ def gemm_variant():
     L.c3cu_set_gemm_variant(0)
 
 
+def test_gemm_cta_cap_keeps_bits_and_is_per_thread(cuda_device, gemm_variant):
+    """c3cu_set_gemm_max_ctas (the SMs a DP step leaves to its all-reduce during dX) changes only
+    how many clusters share the tiles: with the pair kernel without the split tail (variant 2)
+    the results are bit-identical at any cap. The cap belongs to the thread that sets it: a cap of
+    2 CTAs (one cluster for 128 tiles, tens of times slower) set on another thread leaves this
+    thread's launches at full speed."""
+    import threading
+    from c3_b200 import _lib
+    L = _lib.load()
+    gemm_variant(2)
+    M, N, K = 2048, 4096, 1024
+    X, W, b = _fwd_inputs(M, N, K, 41, cuda_device)
+    ref_Y, ref_mask = linear.forward(X, W, b, "nk")
+
+    def timed():
+        linear.forward(X, W, b, "nk")  # warm
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        Y, mask = linear.forward(X, W, b, "nk")
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e), Y, mask
+
+    try:
+        t_full, _, _ = timed()
+        for cap in (2, 40, 128):
+            _lib.check(L.c3cu_set_gemm_max_ctas(cap), "c3cu_set_gemm_max_ctas")
+            t, Y, mask = timed()
+            assert torch.equal(Y, ref_Y) and torch.equal(mask, ref_mask), f"cap {cap}"
+            if cap == 2:
+                t_cap2 = t
+        _lib.check(L.c3cu_set_gemm_max_ctas(0), "c3cu_set_gemm_max_ctas")
+        assert t_cap2 > 8 * t_full, (t_cap2, t_full)  # the cap took effect on this thread
+        th = threading.Thread(target=lambda: L.c3cu_set_gemm_max_ctas(2))
+        th.start()
+        th.join()
+        t_other, Y, _ = timed()
+        assert torch.equal(Y, ref_Y)
+        assert t_other < t_cap2 / 4, (t_other, t_cap2, t_full)  # another thread's cap did not apply
+        assert L.c3cu_set_gemm_max_ctas(-1) != 0  # refused
+    finally:
+        L.c3cu_set_gemm_max_ctas(0)
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 520, 1000), (517, 1032, 776),
                                    (1024, 768, 4096), (129, 256, 64), (4096, 512, 4096),
                                    (8192, 2560, 4096)])
