@@ -13,7 +13,7 @@ import torch
 
 from . import _lib
 
-_ws_cache: dict[int, torch.Tensor] = {}
+_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _p(t: torch.Tensor | None):
@@ -41,11 +41,15 @@ def _require(t: torch.Tensor, name: str, dtype: torch.dtype, ndim: int):
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Scratch of the column-sum kernels (per-block partial sums), one buffer per (device,
+    stream): launches on different streams never share partials. It is allocated while its
+    stream is current, so the caching allocator orders its reuse on that stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _ws_cache.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    ws = _ws_cache.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _ws_cache[idx] = ws
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _ws_cache[key] = ws
     return ws
 
 

@@ -325,3 +325,35 @@ def test_tuner_picks_and_applies_a_variant(cuda_device, tmp_path):
         assert (np.abs(a - c) <= 2.0 ** -7 * np.maximum(np.abs(a), np.abs(c)) + 1e-5 * np.abs(c).max()).all()
     finally:
         _lib.load().c3cu_gemm_tune_clear()
+
+
+def test_prepass_on_two_streams_at_once(cuda_device):
+    """Two pre-passes in flight on two streams of one device: each has its own partial-sum
+    scratch (per device and stream) and its own strip tickets, so both give the bits of a
+    one-stream run."""
+    M, N = 8192, 4096
+    dY1 = randn((M, N), 0.01, 51).to(cuda_device)
+    dY2 = randn((M, N), 0.01, 52).to(cuda_device)
+    g = torch.Generator().manual_seed(53)
+    m1 = torch.randint(-2 ** 31, 2 ** 31 - 1, (M, N // 32), generator=g, dtype=torch.int32).to(cuda_device)
+    m2 = torch.randint(-2 ** 31, 2 ** 31 - 1, (M, N // 32), generator=g, dtype=torch.int32).to(cuda_device)
+    r1 = linear.relu_mask_db(dY1, m1)
+    r2 = linear.relu_mask_db(dY2, m2)
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    s1.wait_stream(cur)
+    s2.wait_stream(cur)
+    outs1, outs2 = [], []
+    for _ in range(4):
+        with torch.cuda.stream(s1):
+            outs1.append(linear.relu_mask_db(dY1, m1))
+        with torch.cuda.stream(s2):
+            outs2.append(linear.relu_mask_db(dY2, m2))
+    cur.wait_stream(s1)
+    cur.wait_stream(s2)
+    torch.cuda.synchronize()
+    for (dz, db) in outs1:
+        assert torch.equal(dz, r1[0]) and torch.equal(db, r1[1])
+    for (dz, db) in outs2:
+        assert torch.equal(dz, r2[0]) and torch.equal(db, r2[1])
