@@ -47,8 +47,8 @@ void* allocDevice(size_t bytes) {
   return p;
 }
 
-void freeDevice(void* p) {
-  if (p) cudaFreeAsync(p, t_stream);
+void freeDevice(void* p, cudaStream_t stream) {
+  if (p) cudaFreeAsync(p, stream);
 }
 
 void checkAbi(int rc, const char* what) {

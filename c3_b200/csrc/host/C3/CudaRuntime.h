@@ -19,9 +19,12 @@ void setCurrentStream(cudaStream_t s);
 // True when a CUDA device is usable from this process.
 bool deviceAvailable();
 
-// Stream-ordered allocation on the current device; throws std::runtime_error on failure.
+// Stream-ordered allocation on the current device and the calling thread's current stream;
+// throws std::runtime_error on failure. freeDevice returns the block on `stream`, the stream it
+// was allocated on: work on other streams must be ordered before the release by the host (as
+// with any stream-ordered allocator), and the stream must outlive the block.
 void* allocDevice(size_t bytes);
-void freeDevice(void* p);
+void freeDevice(void* p, cudaStream_t stream);
 
 // Throws std::runtime_error("<what>: <message>") when rc != 0 (a C3CU_ERR_* status).
 void checkAbi(int rc, const char* what);

@@ -10,10 +10,14 @@ struct Tensor::Storage {
   size_t bytes = 0;
   DeviceType device = DeviceType::kCPU;
   bool owned = true;
+  // Device memory is stream-ordered on the stream it was allocated on (the allocating
+  // thread's current stream) and goes back to the pool on that stream, whichever thread
+  // or current stream releases the last reference.
+  cudaStream_t stream = nullptr;
   ~Storage() {
     if (!owned || !ptr) return;
     if (device == DeviceType::kCUDA)
-      ct::c3::cuda::freeDevice(ptr);
+      ct::c3::cuda::freeDevice(ptr, stream);
     else
       std::free(ptr);
   }
@@ -25,6 +29,7 @@ Tensor::Tensor(ShapeTag, const std::vector<size_t>& shape, DType dtype, DeviceTy
   st->bytes = numel() * dtypeSize(dtype);
   st->device = device;
   if (device == DeviceType::kCUDA) {
+    st->stream = ct::c3::cuda::currentStream();
     st->ptr = ct::c3::cuda::allocDevice(st->bytes);
   } else {
     const size_t rounded = ((st->bytes + 63) / 64) * 64;
