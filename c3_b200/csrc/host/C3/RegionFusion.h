@@ -47,7 +47,8 @@ class RegionFusionRegistry {
                        const std::vector<size_t>& out_numels,
                        const std::vector<std::vector<size_t>>& first_input_shapes = {});
 
-  // Entry for `hash` when active (the pointer stays valid until clear()/uninstallAll()).
+  // Entry for `hash` when active. The entry is immutable and the pointer stays valid until
+  // clear()/uninstallAll(), even if the key is reinstalled meanwhile.
   RegionEntry* find(uint64_t hash);
   RegionEntry* matchFromPosition(const std::vector<uint64_t>& prefix_hashes, size_t current_pos,
                                  const std::vector<size_t>& input_shapes);
@@ -67,9 +68,14 @@ class RegionFusionRegistry {
   RegionFusionRegistry& operator=(const RegionFusionRegistry&) = delete;
 
   void markLastOp(const std::vector<op>& op_seq);
+  void publish(uint64_t hash, RegionEntry&& e);
 
   mutable std::mutex mutex_;
-  std::unordered_map<uint64_t, RegionEntry> entries_;
+  // Published entries are immutable: a reinstall under the same key publishes a new entry and
+  // the superseded one stays in `storage_` until clear(), so a pointer find() returned is never
+  // written while a dispatcher reads it (e.g. the tuned tier replacing the precompiled one).
+  std::unordered_map<uint64_t, RegionEntry*> entries_;
+  std::vector<std::unique_ptr<RegionEntry>> storage_;
   std::atomic<size_t> installed_count_{0};
   static_assert(static_cast<size_t>(op::kCount) <= 64, "op::kCount exceeds the bitmask");
   std::atomic<uint64_t> installed_last_ops_{0};

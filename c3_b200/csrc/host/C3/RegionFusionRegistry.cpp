@@ -9,6 +9,12 @@ RegionFusionRegistry& RegionFusionRegistry::getInstance() {
   return instance;
 }
 
+// Caller holds mutex_.
+void RegionFusionRegistry::publish(uint64_t hash, RegionEntry&& e) {
+  storage_.push_back(std::make_unique<RegionEntry>(std::move(e)));
+  entries_[hash] = storage_.back().get();
+}
+
 void RegionFusionRegistry::markLastOp(const std::vector<op>& op_seq) {
   if (!op_seq.empty())
     installed_last_ops_.fetch_or(uint64_t(1) << static_cast<size_t>(op_seq.back()), std::memory_order_release);
@@ -27,7 +33,7 @@ void RegionFusionRegistry::install(uint64_t hash, const std::vector<op>& op_seq,
   e.num_external_inputs = input_shapes.empty() ? 0 : 1;
   e.len = op_seq.size();
   e.active = true;
-  entries_[hash] = std::move(e);
+  publish(hash, std::move(e));
   markLastOp(op_seq);
 }
 
@@ -63,14 +69,14 @@ void RegionFusionRegistry::installWithCost(const std::vector<op>& op_seq, std::s
   // active only with complete numels and a worthwhile cost estimate; the last-op mask is set
   // regardless (it is only a fast filter).
   e.active = (out_numels.size() == op_seq.size()) && cost.worthwhile;
-  entries_[hash] = std::move(e);
+  publish(hash, std::move(e));
   markLastOp(op_seq);
 }
 
 RegionEntry* RegionFusionRegistry::find(uint64_t hash) {
   std::lock_guard<std::mutex> lock(mutex_);
   auto it = entries_.find(hash);
-  return (it != entries_.end() && it->second.active) ? &it->second : nullptr;
+  return (it != entries_.end() && it->second->active) ? it->second : nullptr;
 }
 
 RegionEntry* RegionFusionRegistry::matchFromPosition(const std::vector<uint64_t>& prefix_hashes,
@@ -83,7 +89,7 @@ RegionEntry* RegionFusionRegistry::matchFromPosition(const std::vector<uint64_t>
   for (size_t len = max_len; len >= 2; --len) {
     const uint64_t h = RollingHash::getSubHash(prefix_hashes, current_pos, current_pos + len - 1);
     auto it = entries_.find(h);
-    if (it != entries_.end() && it->second.active && it->second.len == len) return &it->second;
+    if (it != entries_.end() && it->second->active && it->second->len == len) return it->second;
   }
   return nullptr;
 }
@@ -101,6 +107,7 @@ bool RegionFusionRegistry::mayMatchAsLastOp(op last_op) const {
 void RegionFusionRegistry::clear() {
   std::lock_guard<std::mutex> lock(mutex_);
   entries_.clear();
+  storage_.clear();
   installed_last_ops_.store(0, std::memory_order_release);
   installed_count_.store(0, std::memory_order_release);
 }

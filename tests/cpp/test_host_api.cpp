@@ -9,6 +9,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <array>
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <functional>
 #include <random>
@@ -54,6 +56,7 @@ using c3::FusionCostModel;
 using c3::Graph;
 using c3::HotPathConfig;
 using c3::KernelShapeInfo;
+using c3::RegionEntry;
 using c3::RegionFusionRegistry;
 using c3::RollingHash;
 using c3::TensorDesc;
@@ -191,6 +194,95 @@ TEST(gemm2_schedule_covers_every_tile_once, false) {
   CHECK(dw.sk_mode == 1 && dw.sk_first == 222 && dw.clusters == 74);
   // K = 2048 (32 blocks) never splits
   CHECK(c3cu::gemm2::plan_split(256, 74, 32, 0, split_slots).sk_mode == 0);
+}
+
+// Kernel for the concurrency stress test: an atomic call count, output filled with its level.
+class CountingKernel : public CompiledKernel {
+ public:
+  CountingKernel(int level, std::vector<size_t> out) : out_(std::move(out)) { opt_level_ = level; }
+  std::vector<Tensor> execute(const std::vector<Tensor>&) override {
+    calls.fetch_add(1, std::memory_order_relaxed);
+    Tensor t(ShapeTag{}, out_, DType::kFloat, DeviceType::kCPU);
+    for (size_t i = 0; i < t.numel(); ++i) t.data_write<float>()[i] = static_cast<float>(opt_level_);
+    return {t};
+  }
+  const std::string& cacheKey() const override { return key_; }
+  DeviceType targetDevice() const override { return DeviceType::kCPU; }
+  size_t workspaceBytes() const override { return 0; }
+  std::atomic<int> calls{0};
+
+ private:
+  std::vector<size_t> out_;
+  std::string key_ = "counting";
+};
+
+// Dispatch threads look kernels up and run them while a compile thread installs ever higher
+// tiers into the single-op registry and reinstalls the same region key, as the reference's
+// background compiles do (a tuned tier replacing the precompiled one). Checks: no dispatcher
+// ever sees an uninstalled op or a half-written entry, tiers only move up for each dispatcher,
+// hit counters add up, and the last install wins. Under ThreadSanitizer (tests run the binary
+// built with -fsanitize=thread on this test) it also shows the registries free of data races.
+TEST(registries_concurrent_install_and_dispatch, false) {
+  auto& reg = C3KernelRegistry::getInstance();
+  auto& rr = RegionFusionRegistry::getInstance();
+  reg.uninstallAll();
+  rr.clear();
+  const KernelShapeInfo info{{4, 4}, {4, 4}, {4, 4}};
+  const std::vector<op> seq{op::MatMul, op::Add, op::ReLU};
+  const std::vector<std::vector<size_t>> shapes{{4, 4}, {4, 4}};
+  const uint64_t rkey = RegionFusionRegistry::regionKey(seq, shapes);
+  std::mt19937 rng(3);
+  const Tensor a = hostTensor({4, 4}, rng, -1, 1), b = hostTensor({4, 4}, rng, -1, 1);
+  constexpr int kReaders = 6, kIters = 2000, kLevels = 8;
+  std::vector<std::shared_ptr<CountingKernel>> kernels;
+  for (int l = 1; l <= kLevels; ++l) kernels.push_back(std::make_shared<CountingKernel>(l, std::vector<size_t>{4, 4}));
+  std::atomic<bool> go{false};
+  std::atomic<long> hits{0}, region_runs{0}, bad{0};
+  const size_t hits_before = reg.getStats().hit_count;
+  std::vector<std::thread> threads;
+  for (int r = 0; r < kReaders; ++r)
+    threads.emplace_back([&] {
+      while (!go.load()) std::this_thread::yield();
+      int last = 0;
+      for (int i = 0; i < kIters; ++i) {
+        if (auto out = reg.tryExecute(op::Add, a, b)) {
+          const int v = static_cast<int>(out->data_read<float>()[0]);
+          hits.fetch_add(1);
+          if (v < last || v < 1 || v > kLevels) bad.fetch_add(1);
+          last = v;
+        }
+        if (reg.tryExecute(op::Div, a, b)) bad.fetch_add(1);  // never installed
+        if (rr.mayMatchAsLastOp(op::ReLU)) {
+          if (RegionEntry* e = rr.find(rkey)) {
+            std::shared_ptr<CompiledKernel> k = e->kernel;  // the read a host dispatcher makes
+            if (!k || e->op_seq != seq || !e->active)
+              bad.fetch_add(1);
+            else if (k->execute({a, b}).size() == 1)
+              region_runs.fetch_add(1);
+          }
+        }
+      }
+    });
+  threads.emplace_back([&] {
+    while (!go.load()) std::this_thread::yield();
+    for (int l = 0; l < kLevels; ++l) {
+      reg.install(op::Add, DeviceType::kCPU, kernels[l], info);   // preempts the previous tier
+      reg.install(op::Add, DeviceType::kCPU, kernels[0], info);   // lower tier: ignored
+      rr.installWithCost(seq, kernels[l], {16, 16, 16}, shapes);  // reinstall under the same key
+      std::this_thread::sleep_for(std::chrono::microseconds(300));
+    }
+  });
+  go.store(true);
+  for (auto& t : threads) t.join();
+  CHECK(bad.load() == 0);
+  CHECK(hits.load() > 0 && region_runs.load() > 0);
+  CHECK(reg.getStats().hit_count - hits_before == static_cast<size_t>(hits.load()));
+  auto final_out = reg.tryExecute(op::Add, a, b);
+  CHECK(final_out && final_out->data_read<float>()[0] == static_cast<float>(kLevels));
+  RegionEntry* e = rr.find(rkey);
+  CHECK(e != nullptr && e->kernel == kernels.back());
+  reg.uninstallAll();
+  rr.clear();
 }
 
 TEST(rolling_hash_known_answers, false) {
@@ -605,9 +697,11 @@ TEST(gpu_two_tier_matmul_tuned_tier, true) {
 
 int main(int argc, char** argv) {
   const bool gpu = argc > 1 && std::string(argv[1]) == "--gpu";
+  // --only NAME: run that test alone (e.g. the concurrency test under ThreadSanitizer)
+  const std::string only = (argc > 3 && std::string(argv[2]) == "--only") ? argv[3] : "";
   int ran = 0;
   for (auto& t : registry()) {
-    if (t.gpu != gpu) continue;
+    if (t.gpu != gpu || (!only.empty() && only != t.name)) continue;
     const int before = g_failures;
     try {
       t.fn();

@@ -1,9 +1,12 @@
 """Runs the C++ host-API tests (tests/cpp/test_host_api.cpp) that need no GPU: known answers
 of the rolling hash / region key / cost model derived from the reference code, registry
 install-preemption-fallback semantics, graph lowering, hot-path trigger, backward keys."""
+import os
 import subprocess
 
-from tests.cpp.build import build
+import pytest
+
+from tests.cpp.build import build, build_tsan
 
 
 def test_host_api_cpu():
@@ -12,3 +15,19 @@ def test_host_api_cpu():
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "0 failures" in r.stdout
+
+
+def test_registries_concurrency_under_thread_sanitizer():
+    """The registries' concurrency test (dispatch threads against a compile thread installing
+    and reinstalling kernels) with the host mirror built under ThreadSanitizer: any data race
+    in the registries fails it."""
+    exe = build_tsan()
+    if exe is None:
+        pytest.skip("g++ -fsanitize=thread unavailable")
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1 exitcode=66 second_deadlock_stack=1")
+    r = subprocess.run([str(exe), "--cpu", "--only", "registries_concurrent_install_and_dispatch"],
+                       capture_output=True, text=True, timeout=600, env=env)
+    print(r.stdout)
+    assert "ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
+    assert r.returncode == 0, r.stdout + r.stderr[-4000:]
+    assert "1 tests" in r.stdout and "0 failures" in r.stdout
