@@ -285,6 +285,65 @@ TEST(registries_concurrent_install_and_dispatch, false) {
   rr.clear();
 }
 
+// Several dispatch threads record MatMul -> Add -> ReLU sequences of their own shapes into the
+// hot-path manager (one ring buffer for all threads) while its background compiles install the
+// detected regions, and query both registries as they go. Checks: every region a dispatcher
+// finds is complete, compiles were triggered and all finish, and the counters add up. Run under
+// ThreadSanitizer too (with the registries' test) for the manager's own locking.
+TEST(hot_path_concurrent_record_and_compile, false) {
+  auto& hp = C3HotPathManager::instance();
+  hp.clear();
+  HotPathConfig cfg;
+  cfg.hot_threshold = 2;
+  hp.configure(cfg);
+  auto& rr = RegionFusionRegistry::getInstance();
+  auto& reg = C3KernelRegistry::getInstance();
+  rr.clear();
+  reg.uninstallAll();
+  constexpr int kThreads = 4, kRounds = 150;
+  std::atomic<bool> go{false};
+  std::atomic<long> found{0}, bad{0};
+  const size_t tracked_before = hp.getStats().calls_tracked;
+  std::vector<std::thread> threads;
+  for (int t = 0; t < kThreads; ++t)
+    threads.emplace_back([&, t] {
+      while (!go.load()) std::this_thread::yield();
+      const size_t M = 64 * static_cast<size_t>(t + 1);
+      const uint64_t key = RegionFusionRegistry::regionKey({op::MatMul, op::Add, op::ReLU}, {{M, 784}, {784, 256}});
+      for (int i = 0; i < kRounds; ++i) {
+        hp.recordCall(op::MatMul, DeviceType::kCUDA, {M, 784}, {784, 256}, true);
+        hp.recordCall(op::Add, DeviceType::kCUDA, {M, 256}, {256}, true);
+        hp.recordCall(op::ReLU, DeviceType::kCUDA, {M, 256}, {}, true);
+        if (rr.mayMatchAsLastOp(op::ReLU)) {
+          if (RegionEntry* e = rr.find(key)) {
+            std::shared_ptr<CompiledKernel> k = e->kernel;
+            if (e->len != 3 || !k || !e->cost.worthwhile) bad.fetch_add(1); else found.fetch_add(1);
+          }
+        }
+        (void)reg.findFusedKernelForSequence({op::MatMul, op::Add, op::ReLU}, DeviceType::kCUDA, {M, 784});
+        (void)hp.getStats();
+      }
+    });
+  go.store(true);
+  for (auto& th : threads) th.join();
+  hp.waitForPendingCompiles();
+  const auto st = hp.getStats();
+  CHECK(bad.load() == 0);
+  CHECK(st.calls_tracked - tracked_before == static_cast<size_t>(kThreads) * kRounds * 3);
+  CHECK(st.pending_compiles == 0);
+  // at least one thread's own shapes end up installed (its sequence is found uninterleaved)
+  size_t installed = 0;
+  for (int t = 0; t < kThreads; ++t) {
+    const size_t M = 64 * static_cast<size_t>(t + 1);
+    installed += rr.find(RegionFusionRegistry::regionKey({op::MatMul, op::Add, op::ReLU}, {{M, 784}, {784, 256}})) != nullptr;
+  }
+  CHECK(installed >= 1);
+  hp.shutdown();
+  hp.clear();
+  rr.clear();
+  reg.uninstallAll();
+}
+
 TEST(rolling_hash_known_answers, false) {
   // ((13*131)+2)*131+29 for {MatMul, Add, ReLU} (codes MatMul 13, Add 2, ReLU 29)
   CHECK(RollingHash::hashSequence({op::MatMul, op::Add, op::ReLU}) == 223384ull);

@@ -18,16 +18,18 @@ def test_host_api_cpu():
 
 
 def test_registries_concurrency_under_thread_sanitizer():
-    """The registries' concurrency test (dispatch threads against a compile thread installing
-    and reinstalling kernels) with the host mirror built under ThreadSanitizer: any data race
-    in the registries fails it."""
+    """The concurrency tests (dispatch threads against a compile thread installing and
+    reinstalling kernels; dispatch threads recording into the hot-path manager while its
+    background compiles install regions) with the host mirror built under ThreadSanitizer: any
+    data race in the registries or the manager fails them."""
     exe = build_tsan()
     if exe is None:
         pytest.skip("g++ -fsanitize=thread unavailable")
     env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1 exitcode=66 second_deadlock_stack=1")
-    r = subprocess.run([str(exe), "--cpu", "--only", "registries_concurrent_install_and_dispatch"],
-                       capture_output=True, text=True, timeout=600, env=env)
-    print(r.stdout)
-    assert "ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
-    assert r.returncode == 0, r.stdout + r.stderr[-4000:]
-    assert "1 tests" in r.stdout and "0 failures" in r.stdout
+    for name in ("registries_concurrent_install_and_dispatch", "hot_path_concurrent_record_and_compile"):
+        r = subprocess.run([str(exe), "--cpu", "--only", name], capture_output=True, text=True, timeout=600,
+                           env=env)
+        print(r.stdout)
+        assert "ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
+        assert r.returncode == 0, r.stdout + r.stderr[-4000:]
+        assert "1 tests" in r.stdout and "0 failures" in r.stdout
