@@ -545,6 +545,47 @@ TEST(fused_backward_sequence_detection, false) {
         !C3BackwardCapture::isElementWiseBackward(typeid(::AddNode).name()));
 }
 
+// Backward capture from several autograd threads at once: each records Sigmoid -> Tanh
+// backward pairs of its own shape (one recording window for all threads) while fused-backward
+// compiles run in the background, and probes the registry for its fused key. Checks: compiles
+// finish, at least one thread's pair is installed under its exact key, and no probe sees a
+// partial entry. Run under ThreadSanitizer too.
+TEST(backward_capture_concurrent_recording, false) {
+  auto& bc = C3BackwardCapture::getInstance();
+  auto& reg = C3KernelRegistry::getInstance();
+  bc.clear();
+  reg.uninstallAll();
+  const std::string sig = typeid(::SigmoidNode).name(), tanh_t = typeid(::TanhNode).name();
+  constexpr int kThreads = 4, kRounds = 100;
+  std::atomic<bool> go{false};
+  std::vector<std::thread> threads;
+  for (int t = 0; t < kThreads; ++t)
+    threads.emplace_back([&, t] {
+      while (!go.load()) std::this_thread::yield();
+      const std::vector<size_t> shp{16 * static_cast<size_t>(t + 1), 64};
+      Tensor x(ShapeTag{}, shp, DType::kFloat, DeviceType::kCPU);
+      const std::string key = C3BackwardCapture::makeFusedBackwardKey("Sigmoid+Tanh", shp, shp);
+      for (int i = 0; i < kRounds; ++i) {
+        bc.recordBackwardNode(sig, shp, shp, {x});
+        bc.recordBackwardNode(tanh_t, shp, shp, {x});
+        (void)reg.hasBackwardKey(key);
+        (void)bc.getStats();
+      }
+    });
+  go.store(true);
+  for (auto& th : threads) th.join();
+  bc.waitForPendingCompiles();
+  size_t installed = 0;
+  for (int t = 0; t < kThreads; ++t) {
+    const std::vector<size_t> shp{16 * static_cast<size_t>(t + 1), 64};
+    installed += reg.hasBackwardKey(C3BackwardCapture::makeFusedBackwardKey("Sigmoid+Tanh", shp, shp));
+  }
+  CHECK(installed >= 1);
+  CHECK(bc.getStats().fusion_compile_count >= 1);
+  bc.clear();
+  reg.uninstallAll();
+}
+
 // ============================================================================ GPU
 TEST(gpu_region_fp32_is_bit_exact_through_registry, true) {
   // cfg1 layer shapes: the fp32 path reproduces the reference's loop arithmetic exactly.
