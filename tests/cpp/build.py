@@ -33,17 +33,18 @@ def build() -> Path:
     return OUT
 
 
-TSAN_OUT = HERE / "_build" / "test_host_api_tsan"
+SANITIZERS = {"thread": "test_host_api_tsan", "address,undefined": "test_host_api_asan"}
 
 
-def build_tsan() -> Path | None:
-    """The same test program with the C++ host mirror compiled in under ThreadSanitizer
-    (-fsanitize=thread), for the registries' concurrency test. The C ABI and the oracle come
-    from their libraries as usual (only the host sources are instrumented). Returns None when
-    this toolchain cannot build it."""
+def build_sanitized(sanitize: str = "thread") -> Path | None:
+    """The same test program with the C++ host mirror compiled in under a sanitizer
+    (`-fsanitize=thread` for data races; `-fsanitize=address,undefined` for memory errors, leaks
+    and undefined behaviour). The C ABI and the oracle come from their libraries as usual (only
+    the host sources are instrumented). Returns None when this toolchain cannot build it."""
     sys.path.insert(0, str(ROOT))
     from c3_b200 import build as lib_build
     import oracle
+    out = HERE / "_build" / SANITIZERS[sanitize]
     lib = lib_build.build()
     olib = oracle.build()
     src = HERE / "test_host_api.cpp"
@@ -51,19 +52,24 @@ def build_tsan() -> Path | None:
     host_srcs = sorted(host.rglob("*.cpp"))
     headers = list(host.rglob("*.h")) + [ROOT / "include" / "c3cu.h", ROOT / "c3_b200" / "csrc" / "gemm2_schedule.h"]
     deps = [src, lib, olib] + headers + host_srcs
-    if TSAN_OUT.exists() and all(TSAN_OUT.stat().st_mtime >= p.stat().st_mtime for p in deps):
-        return TSAN_OUT
-    TSAN_OUT.parent.mkdir(exist_ok=True)
-    cmd = ["g++", "-std=c++17", "-O1", "-g", "-fsanitize=thread", "-pthread", str(src)] + [str(p) for p in host_srcs] + \
-          ["-o", str(TSAN_OUT), f"-I{host}", f"-I{ROOT / 'c3_b200' / 'csrc'}", f"-I{ROOT / 'include'}",
+    if out.exists() and all(out.stat().st_mtime >= p.stat().st_mtime for p in deps):
+        return out
+    out.parent.mkdir(exist_ok=True)
+    cmd = ["g++", "-std=c++17", "-O1", "-g", f"-fsanitize={sanitize}", "-fno-omit-frame-pointer", "-pthread",
+           str(src)] + [str(p) for p in host_srcs] + \
+          ["-o", str(out), f"-I{host}", f"-I{ROOT / 'c3_b200' / 'csrc'}", f"-I{ROOT / 'include'}",
            "-I/usr/local/cuda/include", f"-L{lib.parent}", "-lc3cu", f"-Wl,-rpath,{lib.parent}",
            f"-L{olib.parent}", "-loracle", f"-Wl,-rpath,{olib.parent}", "-L/usr/local/cuda/lib64", "-lcudart",
            "-Wl,-rpath,/usr/local/cuda/lib64"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        print(f"ThreadSanitizer build unavailable: {r.stderr[-2000:]}")
+        print(f"-fsanitize={sanitize} build unavailable: {r.stderr[-2000:]}")
         return None
-    return TSAN_OUT
+    return out
+
+
+def build_tsan() -> Path | None:
+    return build_sanitized("thread")
 
 
 if __name__ == "__main__":
