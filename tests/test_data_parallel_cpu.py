@@ -253,3 +253,48 @@ def test_mlp_shard_batch_needs_equal_shares():
     assert mlp.shard_batch(128, 4, 3) == (96, 128)
     with pytest.raises(ValueError):
         mlp.shard_batch(128, 3, 0)
+
+
+# Property tests of the shard arithmetic over arbitrary sizes and world sizes.
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=300, deadline=None)
+@given(n=st.integers(0, 1 << 40), world=st.integers(1, 64), align=st.sampled_from([1, 2, 4, 8, 16]))
+def test_shard_range_properties(n, world, align):
+    ranges = [shard_range(n, world, r, align) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0
+    for lo, hi in ranges:
+        assert 0 <= lo <= hi <= n
+        assert lo % align == 0 or lo == n
+    vecs = [(hi - lo + align - 1) // align for lo, hi in ranges]
+    assert max(vecs) - min(vecs) <= 1
+
+
+@settings(max_examples=300, deadline=None)
+@given(m=st.integers(0, 1 << 40), world=st.integers(1, 64))
+def test_shard_rows_properties(m, world):
+    ranges = [shard_rows(m, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == m
+    sizes = [hi - lo for lo, hi in ranges]
+    assert all(s >= 0 for s in sizes) and max(sizes) - min(sizes) <= 1 and sum(sizes) == m
+
+
+@settings(max_examples=200, deadline=None)
+@given(b=st.integers(0, 64), h=st.integers(0, 128), world=st.integers(1, 16))
+def test_shard_heads_properties(b, h, world):
+    covered = [i for r in range(world) for i in range(*shard_heads(b, h, world, r))]
+    assert covered == list(range(b * h))
+
+
+@settings(max_examples=200, deadline=None)
+@given(n=st.integers(1, 1 << 16), chunks=st.integers(0, 16))
+def test_dw_bands_properties(n, chunks):
+    bands = dw_bands(n, chunks)
+    assert bands[0][0] == 0 and bands[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(bands, bands[1:]):
+        assert a1 == b0
+    if len(bands) > 1:
+        assert all((hi - lo) % 8 == 0 for lo, hi in bands) and len(bands) == chunks
