@@ -1,0 +1,79 @@
+"""Property tests of the oracle (oracle/c3_oracle.c, test infrastructure) over random shapes,
+against independent numpy restatements of the reference's fp32 loops:
+
+- c3.matmul (src/C3/C3DialectLowering.cpp:467-610): out[i,j] = ((0 + a_i0*b_0j) + a_i1*b_1j) + ...,
+  k ascending, a separate fp32 rounding after every multiply and every add. numpy float32
+  arithmetic rounds each elementwise operation to fp32, so a k loop over float32 arrays is the
+  same computation; transposes only change the indexing (transA: A stored [K, M]; transB: B
+  stored [N, K]).
+- the region (src/C3/MLIRKernelGen.cpp:610-768): z = T + b[j % numel(b)], out = maxnum(z, 0).
+- ReLU backward Mul(Gt(x, 0), grad) (src/C3/C3BackwardCapture.cpp:501-528) and SumReduce axis 0,
+  i ascending (src/C3/C3DialectLowering.cpp:382-465).
+
+All comparisons are bit-exact."""
+import numpy as np
+from hypothesis import given, settings, strategies as st
+
+import oracle
+
+
+def _seq_k_matmul(A, B, ta, tb):
+    A = A.T if ta else A  # logical [M, K]
+    B = B.T if tb else B  # logical [K, N]
+    M, K = A.shape
+    N = B.shape[1]
+    acc = np.zeros((M, N), np.float32)
+    for k in range(K):
+        acc = acc + A[:, k:k + 1] * B[k:k + 1, :]  # float32 multiply, then float32 add
+    return acc
+
+
+def _rand(rng, shape, scale=1.0):
+    return (rng.standard_normal(shape) * scale).astype(np.float32)
+
+
+def _bits_equal(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+@settings(max_examples=60, deadline=None)
+@given(M=st.integers(1, 24), K=st.integers(1, 40), N=st.integers(1, 24), ta=st.booleans(), tb=st.booleans(),
+       seed=st.integers(0, 2 ** 31 - 1))
+def test_matmul_is_sequential_k_fp32(M, K, N, ta, tb, seed):
+    rng = np.random.default_rng(seed)
+    A = _rand(rng, (K, M) if ta else (M, K))
+    B = _rand(rng, (N, K) if tb else (K, N))
+    out = oracle.matmul(A, B, transA=ta, transB=tb)
+    assert _bits_equal(out, _seq_k_matmul(A, B, ta, tb))
+
+
+@settings(max_examples=60, deadline=None)
+@given(M=st.integers(1, 24), K=st.integers(1, 40), N=st.integers(1, 24),
+       bias_kind=st.sampled_from(["row", "scalar"]), seed=st.integers(0, 2 ** 31 - 1))
+def test_region_is_bias_after_the_k_sum_then_maxnum(M, K, N, bias_kind, seed):
+    rng = np.random.default_rng(seed)
+    X, B = _rand(rng, (M, K)), _rand(rng, (K, N), 0.3)
+    b = _rand(rng, (N,) if bias_kind == "row" else (1,), 0.1)
+    out, z = oracle.region_fwd(X, B, b)
+    T = _seq_k_matmul(X, B, False, False)
+    z_ref = T + np.broadcast_to(b, (N,)) if b.size == N else T + b[0]
+    assert _bits_equal(z, z_ref)
+    # maxnum(z, 0): z where z > 0, else +0 or -0; compare values (signed zeros both count as 0)
+    ref = np.where(z_ref > 0, z_ref, np.float32(0))
+    assert np.array_equal(out, ref)
+
+
+@settings(max_examples=60, deadline=None)
+@given(M=st.integers(1, 64), N=st.integers(1, 48), seed=st.integers(0, 2 ** 31 - 1))
+def test_relu_backward_and_sum_reduce_orders(M, N, seed):
+    rng = np.random.default_rng(seed)
+    grad, x = _rand(rng, (M, N)), _rand(rng, (M, N))
+    x[rng.random((M, N)) < 0.1] = 0.0  # Gt(0, 0) is false: the gradient is zeroed
+    dz = oracle.relu_bwd(grad, x)
+    dz_ref = np.where(x > 0, np.float32(1), np.float32(0)) * grad
+    assert _bits_equal(dz, dz_ref)
+    db = oracle.sum_reduce(np.ascontiguousarray(dz.reshape(M, N)), 0)
+    acc = np.zeros(N, np.float32)
+    for i in range(M):
+        acc = acc + dz_ref.reshape(M, N)[i]
+    assert _bits_equal(db, acc)
