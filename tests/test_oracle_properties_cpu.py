@@ -9,8 +9,13 @@ against independent numpy restatements of the reference's fp32 loops:
 - the region (src/C3/MLIRKernelGen.cpp:610-768): z = T + b[j % numel(b)], out = maxnum(z, 0).
 - ReLU backward Mul(Gt(x, 0), grad) (src/C3/C3BackwardCapture.cpp:501-528) and SumReduce axis 0,
   i ascending (src/C3/C3DialectLowering.cpp:382-465).
+- the fused backward chains: the reference's per-type gradient graphs chained upstream, with
+  libm's expf (called through ctypes, as the reference's JIT calls it).
 
 All comparisons are bit-exact."""
+import ctypes
+import ctypes.util
+
 import numpy as np
 from hypothesis import given, settings, strategies as st
 
@@ -77,3 +82,58 @@ def test_relu_backward_and_sum_reduce_orders(M, N, seed):
     for i in range(M):
         acc = acc + dz_ref.reshape(M, N)[i]
     assert _bits_equal(db, acc)
+
+
+_libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+_libm.expf.restype = ctypes.c_float
+_libm.expf.argtypes = [ctypes.c_float]
+_expf_v = np.vectorize(lambda v: _libm.expf(v), otypes=[np.float32])
+
+
+def _expf(x):
+    # libm's expf, the function the reference's JIT calls (math.exp lowers to it)
+    return _expf_v(x.astype(np.float32)).astype(np.float32)
+
+
+def _chain_ref(types, grad, xs):
+    """The reference's per-type backward graphs (src/C3/C3BackwardCapture.cpp:501-617 ReLU,
+    Sigmoid, Tanh; 725-743 Neg; 823-872 Exp, Log), one fp32 operation per graph node, chained
+    from the most downstream node upstream."""
+    g = grad.astype(np.float32)
+    outs = []
+    one = np.float32(1)
+    for t, x in zip(types, xs):
+        x = np.zeros_like(g) if x is None else x.astype(np.float32)
+        if t == "ReLU":
+            r = np.where(x > 0, one, np.float32(0)) * g
+        elif t == "Sigmoid":
+            s = one / (one + _expf(-x))
+            r = g * (s * (one - s))
+        elif t == "Tanh":
+            ep, en = _expf(x), _expf(-x)
+            th = (ep - en) / (ep + en)
+            r = g * (one - th * th)
+        elif t == "Neg":
+            r = -g
+        elif t == "Exp":
+            r = _expf(x) * g
+        elif t == "Log":
+            r = g / x
+        outs.append(r.astype(np.float32))
+        g = outs[-1]
+    return outs
+
+
+@settings(max_examples=80, deadline=None)
+@given(types=st.lists(st.sampled_from(["ReLU", "Sigmoid", "Tanh", "Neg", "Exp", "Log"]), min_size=1, max_size=5),
+       n=st.integers(1, 300), seed=st.integers(0, 2 ** 31 - 1))
+def test_backward_chain_follows_the_per_type_graphs(types, n, seed):
+    rng = np.random.default_rng(seed)
+    grad = _rand(rng, (n,))
+    # Log's input away from 0; Exp/Tanh/Sigmoid inputs in a range where exp stays finite
+    xs = [(rng.random(n).astype(np.float32) + np.float32(0.5)) if t == "Log" else _rand(rng, (n,), 2.0)
+          for t in types]
+    got = oracle.backward_chain(types, grad, xs)
+    ref = _chain_ref(types, grad, xs)
+    for k, (g, r) in enumerate(zip(got, ref)):
+        assert _bits_equal(g, r), (types, k, float(np.abs(g - r).max()))
