@@ -137,3 +137,51 @@ def test_backward_chain_follows_the_per_type_graphs(types, n, seed):
     ref = _chain_ref(types, grad, xs)
     for k, (g, r) in enumerate(zip(got, ref)):
         assert _bits_equal(g, r), (types, k, float(np.abs(g - r).max()))
+
+
+_libm.logf.restype = ctypes.c_float
+_libm.logf.argtypes = [ctypes.c_float]
+
+
+@settings(max_examples=60, deadline=None)
+@given(n=st.integers(1, 2000), threads=st.sampled_from([1, 3, 8]), seed=st.integers(0, 2 ** 31 - 1))
+def test_cfg4_chain_elementwise_order(n, threads, seed):
+    """relu((A + B) * C - A) / (1 + exp(-B)) (MLIRKernelGen.cpp:610-768 scalar fused path):
+    Neg, Exp, Add, Add, Mul, Sub, ReLU = maxnum(x, 0), Div, one fp32 operation each; the result
+    does not depend on how the elements are split over host threads."""
+    rng = np.random.default_rng(seed)
+    A = (rng.random(n) * 8 - 4).astype(np.float32)
+    B = (rng.random(n) * 16 - 8).astype(np.float32)
+    C = (rng.random(n) * 8 - 4).astype(np.float32)
+    out = oracle.ew_cfg4(A, B, C, threads=threads)
+    d = np.float32(1) + _expf(-B)
+    t = (A + B) * C - A
+    ref = np.where(t > 0, t, np.float32(0)) / d
+    assert np.array_equal(out, ref)  # values; a ReLU zero may carry either sign
+
+
+@settings(max_examples=40, deadline=None)
+@given(Bn=st.integers(1, 64), C=st.integers(2, 12), seed=st.integers(0, 2 ** 31 - 1))
+def test_softmax_ce_textbook_order(Bn, C, seed):
+    """The textbook softmax cross-entropy in the order the kernels use (max, sum of expf(z - m)
+    c ascending, lse = m + logf(s), loss summed i ascending times 1/B; dz = (expf(z - lse) -
+    onehot) * (1/B)) with libm's expf / logf: bit-exact."""
+    rng = np.random.default_rng(seed)
+    z = _rand(rng, (Bn, C), 3.0)
+    y = rng.integers(0, C, Bn).astype(np.int32)
+    loss, dz = oracle.softmax_ce(z, y)
+    invB = np.float32(1) / np.float32(Bn)
+    total = np.float32(0)
+    dz_ref = np.empty_like(z)
+    for i in range(Bn):
+        m = z[i].max()
+        s = np.float32(0)
+        for c in range(C):
+            s = np.float32(s + _libm.expf(np.float32(z[i, c] - m)))
+        lse = np.float32(m + np.float32(_libm.logf(s)))
+        total = np.float32(total + np.float32(lse - z[i, y[i]]))
+        for c in range(C):
+            p = np.float32(_libm.expf(np.float32(z[i, c] - lse)))
+            dz_ref[i, c] = np.float32(np.float32(p - (1 if c == y[i] else 0)) * invB)
+    assert np.float32(loss) == np.float32(total * invB)
+    assert _bits_equal(dz, dz_ref)
