@@ -185,3 +185,26 @@ def test_softmax_ce_textbook_order(Bn, C, seed):
             dz_ref[i, c] = np.float32(np.float32(p - (1 if c == y[i] else 0)) * invB)
     assert np.float32(loss) == np.float32(total * invB)
     assert _bits_equal(dz, dz_ref)
+
+
+@settings(max_examples=40, deadline=None)
+@given(S=st.integers(1, 96), D=st.sampled_from([8, 16, 64, 128]), causal=st.booleans(),
+       seed=st.integers(0, 2 ** 31 - 1))
+def test_attention_rows_against_float64(S, D, causal, seed):
+    """The textbook attention the FlashAttention kernel is checked against (no reference code,
+    parity unpinned): O = softmax(scale * Q K^T + causal mask) V and LSE = m + log(sum), here
+    against a float64 numpy evaluation (relative error of O <= 1e-5, LSE <= 1e-5 absolute)."""
+    rng = np.random.default_rng(seed)
+    q, k, v = (_rand(rng, (S, D)) for _ in range(3))
+    scale = 1.0 / np.sqrt(D)
+    o, lse = oracle.attention_rows(q, k, v, scale, causal)
+    s = (q.astype(np.float64) @ k.astype(np.float64).T) * scale
+    if causal:
+        s = np.where(np.tril(np.ones((S, S), bool)), s, -np.inf)
+    m = s.max(axis=1, keepdims=True)
+    p = np.exp(s - m)
+    l = p.sum(axis=1, keepdims=True)
+    o_ref = (p / l) @ v.astype(np.float64)
+    lse_ref = (m + np.log(l))[:, 0]
+    assert np.abs(o - o_ref).max() <= 1e-5 * max(np.abs(o_ref).max(), 1.0)
+    assert np.abs(lse - lse_ref).max() <= 1e-5 * max(np.abs(lse_ref).max(), 1.0)
