@@ -85,7 +85,8 @@ int c3cu_linear_bias_relu_fwd(const void* X, const void* W, const float* bias, v
 
 /* Backward pre-pass: dZ = dY * mask (bf16, exact) and db[n] = sum_m dZ[m][n] (fp32).
  * Needs a device workspace of c3cu_relu_mask_db_workspace(M, N) bytes for the partial
- * column sums. The first call on a (device, stream) allocates a 256 KiB array of reduction
+ * column sums; calls that may run at the same time (different streams) need different
+ * workspaces. The first call on a (device, stream) allocates a 256 KiB array of reduction
  * tickets that the library keeps for that stream (the tickets return to zero after every
  * call, so later calls launch only the kernel). The same holds for c3cu_sum_rows_f32. */
 size_t c3cu_relu_mask_db_workspace(int64_t M, int64_t N);
