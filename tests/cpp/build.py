@@ -40,30 +40,45 @@ def build_sanitized(sanitize: str = "thread") -> Path | None:
     """The same test program with the C++ host mirror compiled in under a sanitizer
     (`-fsanitize=thread` for data races; `-fsanitize=address,undefined` for memory errors, leaks
     and undefined behaviour). The C ABI and the oracle come from their libraries as usual (only
-    the host sources are instrumented). Returns None when this toolchain cannot build it."""
+    the host sources are instrumented). Sources compile in parallel, then link. Returns None
+    when this toolchain cannot build it."""
+    import concurrent.futures as cf
+    import os
     sys.path.insert(0, str(ROOT))
     from c3_b200 import build as lib_build
     import oracle
     out = HERE / "_build" / SANITIZERS[sanitize]
+    objdir = HERE / "_build" / (SANITIZERS[sanitize] + "_obj")
     lib = lib_build.build()
     olib = oracle.build()
     src = HERE / "test_host_api.cpp"
     host = ROOT / "c3_b200" / "csrc" / "host"
-    host_srcs = sorted(host.rglob("*.cpp"))
+    srcs = [src] + sorted(host.rglob("*.cpp"))
     headers = list(host.rglob("*.h")) + [ROOT / "include" / "c3cu.h", ROOT / "c3_b200" / "csrc" / "gemm2_schedule.h"]
-    deps = [src, lib, olib] + headers + host_srcs
-    if out.exists() and all(out.stat().st_mtime >= p.stat().st_mtime for p in deps):
+    if out.exists() and all(out.stat().st_mtime >= p.stat().st_mtime for p in [lib, olib] + headers + srcs):
         return out
-    out.parent.mkdir(exist_ok=True)
-    cmd = ["g++", "-std=c++17", "-O1", "-g", f"-fsanitize={sanitize}", "-fno-omit-frame-pointer", "-pthread",
-           str(src)] + [str(p) for p in host_srcs] + \
-          ["-o", str(out), f"-I{host}", f"-I{ROOT / 'c3_b200' / 'csrc'}", f"-I{ROOT / 'include'}",
-           "-I/usr/local/cuda/include", f"-L{lib.parent}", "-lc3cu", f"-Wl,-rpath,{lib.parent}",
+    objdir.mkdir(parents=True, exist_ok=True)
+    flags = ["g++", "-std=c++17", "-O1", "-g", f"-fsanitize={sanitize}", "-fno-omit-frame-pointer", "-pthread",
+             f"-I{host}", f"-I{ROOT / 'c3_b200' / 'csrc'}", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include"]
+
+    def compile_one(path: Path):
+        obj = objdir / (path.relative_to(ROOT).as_posix().replace("/", "_") + ".o")
+        r = subprocess.run(flags + ["-c", str(path), "-o", str(obj)], capture_output=True, text=True)
+        return obj, r
+
+    with cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
+        results = list(ex.map(compile_one, srcs))
+    for _, r in results:
+        if r.returncode != 0:
+            print(f"-fsanitize={sanitize} build unavailable: {r.stderr[-2000:]}")
+            return None
+    cmd = ["g++", f"-fsanitize={sanitize}", "-pthread"] + [str(o) for o, _ in results] + \
+          ["-o", str(out), f"-L{lib.parent}", "-lc3cu", f"-Wl,-rpath,{lib.parent}",
            f"-L{olib.parent}", "-loracle", f"-Wl,-rpath,{olib.parent}", "-L/usr/local/cuda/lib64", "-lcudart",
            "-Wl,-rpath,/usr/local/cuda/lib64"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        print(f"-fsanitize={sanitize} build unavailable: {r.stderr[-2000:]}")
+        print(f"-fsanitize={sanitize} link failed: {r.stderr[-2000:]}")
         return None
     return out
 
