@@ -2,6 +2,7 @@
 (test infrastructure) into tests/cpp/_build/test_host_api."""
 from __future__ import annotations
 
+import shutil
 import subprocess
 import sys
 from pathlib import Path
@@ -77,6 +78,7 @@ def build_sanitized(sanitize: str = "thread") -> Path | None:
            f"-L{olib.parent}", "-loracle", f"-Wl,-rpath,{olib.parent}", "-L/usr/local/cuda/lib64", "-lcudart",
            "-Wl,-rpath,/usr/local/cuda/lib64"]
     r = subprocess.run(cmd, capture_output=True, text=True)
+    shutil.rmtree(objdir, ignore_errors=True)  # intermediates only; the binary's mtime decides rebuilds
     if r.returncode != 0:
         print(f"-fsanitize={sanitize} link failed: {r.stderr[-2000:]}")
         return None
