@@ -10,7 +10,10 @@
 // 256 x 256 x 16 tcgen05.mma per K step, which reads both CTAs' shared memory and writes
 // each CTA's half of the accumulator rows into that CTA's TMEM.
 //
-// Roles per CTA (6 warps, one CTA per SM):
+// Which tiles (and K ranges) a cluster computes comes from gemm2_schedule.h (work_item), the
+// same header the launcher's split plan and the host-side coverage test use.
+//
+// Roles per CTA (10 warps, one CTA per SM):
 //   warp 0      TMA producer. Both CTAs load their halves; every copy signals the leader's
 //               `full` barrier (the leader arms it with the bytes of both halves).
 //   warp 1      TMEM owner (pair allocation); in the leader also the MMA issuer. Each
