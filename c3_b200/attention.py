@@ -7,7 +7,7 @@ import math
 import torch
 
 from . import _lib
-from .linear import _p, _stream
+from .linear import _p, _require, _stream
 
 
 @_lib.on_tensor_device
@@ -15,18 +15,18 @@ def flash_attn_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bo
                    scale: float | None = None, out: torch.Tensor | None = None,
                    lse: torch.Tensor | None = None):
     """Q, K, V: [B, H, S, 128] bf16 contiguous CUDA tensors. Returns (O bf16, LSE fp32 [B, H, S])."""
-    for t, n in ((Q, "Q"), (K, "K"), (V, "V")):
-        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 4:
-            raise _lib.C3CUError(-1, n, "expected a contiguous [B, H, S, D] bf16 CUDA tensor")
-    if not (Q.shape == K.shape == V.shape):
-        raise _lib.C3CUError(-1, "flash_attn_fwd", "Q, K, V shapes differ")
+    _require(Q, "Q", torch.bfloat16, 4)
     B, H, S, D = Q.shape
+    _require(K, "K", torch.bfloat16, 4, Q.shape)
+    _require(V, "V", torch.bfloat16, 4, Q.shape)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty_like(Q)
+    _require(out, "out", torch.bfloat16, 4, Q.shape)
     if lse is None:
         lse = torch.empty((B, H, S), dtype=torch.float32, device=Q.device)
+    _require(lse, "lse", torch.float32, 3, (B, H, S))
     rc = _lib.load().c3cu_flash_attn_fwd(_p(Q), _p(K), _p(V), _p(out), _p(lse), B, H, S, D, scale,
                                          int(causal), _stream(Q.device))
     _lib.check(rc, "c3cu_flash_attn_fwd")

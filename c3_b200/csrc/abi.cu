@@ -164,6 +164,7 @@ int c3cu_fault_status(uint32_t* code) {
   c3cu_fault_clear_nvls();
   c3cu_fault_clear_train();
   if (*code != 0u) {
+    c3cu::gemm_invalidate_split_workspaces();
     c3cu::set_error("kernel fault recorded: code %u (site %u)", *code & 0xffffu, *code >> 16);
     return C3CU_ERR_FAULT;
   }

@@ -469,7 +469,7 @@ int grid_for(int64_t work_items, int threads, int blocks_per_sm = 8) {
 // library owns. Every GPU that loads the library holds C3CU_NOALLOC_SCRATCH_BYTES of it
 // until the process exits. Host code must not pass `g_noalloc_scratch` itself to a kernel
 // (on the host that name is a stand-in, not a device address): the address is looked up
-// once per device with cudaGetSymbolAddress and cached.
+// once per device (and CUDA context) with cudaGetSymbolAddress and cached.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[C3CU_NOALLOC_SCRATCH_BYTES];
 
 namespace c3cu {
@@ -477,10 +477,40 @@ namespace ew {
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kMaxDevices] = {};
+// The address is cached per device together with the CUDA context it was looked up in: after
+// a cudaDeviceReset the runtime makes a new primary context, the library's module is loaded
+// again and the array may sit elsewhere, so a different current context forces a new lookup.
+struct NoallocSlot {
+  CUcontext ctx;
+  void* addr;
+};
+NoallocSlot g_noalloc[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device; the first call on a device
-// performs the lookup (so it should happen before any stream capture).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+CUcontext current_context() {
+  CUcontext ctx = nullptr;
+  CtxGetCurrentFn f = ctx_get_current_fn();
+  if (f == nullptr || f(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+// Device address of the scratch array on the current device. The first call on a device (and
+// the first after that device's context was replaced) performs the lookup, so it should
+// happen before any stream capture. Without a current context the lookup runs every call.
 int noalloc_scratch(void** out) {
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev), "relu_mask_db_noalloc: cudaGetDevice");
@@ -489,15 +519,19 @@ int noalloc_scratch(void** out) {
     set_error("relu_mask_db_noalloc: device ordinal %d out of range", dev);
     return C3CU_ERR_UNSUPPORTED;
   }
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  NoallocSlot& slot = g_noalloc[dev];
+  if (slot.addr == nullptr || ctx == nullptr || slot.ctx != ctx) {
     void* p = nullptr;
     rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                      "relu_mask_db_noalloc: cudaGetSymbolAddress of the scratch array");
     if (rc != C3CU_OK) return rc;
-    g_noalloc_addr[dev] = p;
+    // the lookup made the runtime's context current if none was
+    slot.ctx = ctx != nullptr ? ctx : current_context();
+    slot.addr = p;
   }
-  *out = g_noalloc_addr[dev];
+  *out = slot.addr;
   return C3CU_OK;
 }
 }  // namespace

@@ -76,30 +76,40 @@ constexpr size_t kSplitPartialFloats = static_cast<size_t>(kSplitMax) * 2 * gemm
 constexpr size_t kSplitWords = static_cast<size_t>(kSplitMax) * 2 * gemm2::kEpiWarps;
 constexpr size_t kSplitWsBytes = kSplitPartialFloats * 4 + 2 * kSplitWords * 4;
 
+// Bumped by gemm_invalidate_split_workspaces (after a recorded fault): a workspace cleared
+// under an older generation is cleared again before its next launch.
+std::atomic<uint32_t> g_split_generation{0};
+
+struct SplitWs {
+  void* ws;
+  uint32_t generation;
+};
+
 int split_workspace(cudaStream_t stream, float** partial, uint32_t** tickets, uint32_t** ready) {
   static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, void*> pool;
+  static std::map<std::pair<int, cudaStream_t>, SplitWs> pool;
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev), "gemm2: current device");
   if (rc != C3CU_OK) return rc;
+  const uint32_t gen = g_split_generation.load(std::memory_order_acquire);
   std::lock_guard<std::mutex> lock(mu);
-  void*& ws = pool[{dev, stream}];
-  if (ws == nullptr) {
-    rc = cuda_status(cudaMalloc(&ws, kSplitWsBytes), "gemm2: split-K workspace");
+  SplitWs& entry = pool[{dev, stream}];
+  if (entry.ws == nullptr) {
+    rc = cuda_status(cudaMalloc(&entry.ws, kSplitWsBytes), "gemm2: split-K workspace");
     if (rc != C3CU_OK) {
-      ws = nullptr;
+      entry.ws = nullptr;
       return rc;
     }
-    // cleared on the stream that will use it, so the clear precedes its first launch even on
-    // a stream that does not synchronise with the legacy default stream
-    rc = cuda_status(cudaMemsetAsync(ws, 0, kSplitWsBytes, stream), "gemm2: clear split-K workspace");
-    if (rc != C3CU_OK) {
-      cudaFree(ws);
-      ws = nullptr;
-      return rc;
-    }
+    entry.generation = gen - 1u;  // forces the clear below
   }
-  *partial = static_cast<float*>(ws);
+  if (entry.generation != gen) {
+    // cleared on the stream that will use it, so the clear precedes its next launch even on
+    // a stream that does not synchronise with the legacy default stream
+    rc = cuda_status(cudaMemsetAsync(entry.ws, 0, kSplitWsBytes, stream), "gemm2: clear split-K workspace");
+    if (rc != C3CU_OK) return rc;
+    entry.generation = gen;
+  }
+  *partial = static_cast<float*>(entry.ws);
   *tickets = reinterpret_cast<uint32_t*>(*partial + kSplitPartialFloats);
   *ready = *tickets + kSplitWords;
   return C3CU_OK;
@@ -226,6 +236,8 @@ int check_common(int64_t M, int64_t N, int64_t K) {
 }
 
 }  // namespace
+
+void gemm_invalidate_split_workspaces() { g_split_generation.fetch_add(1u, std::memory_order_acq_rel); }
 
 int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
                  void* out, int64_t ldo, int epi, const float* bias, uint32_t* mask, int64_t ldm,

@@ -39,6 +39,12 @@ int require_sm100();
 int encode_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                          uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
+// Called by c3cu_fault_status when a kernel recorded a fault: a split-K GEMM whose adder gave
+// up waiting may leave its ticket and ready words non-zero (its partner publishes after the
+// adder has reset them), so every pooled split workspace is cleared again on its stream before
+// its next launch.
+void gemm_invalidate_split_workspaces();
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
 
 }  // namespace c3cu

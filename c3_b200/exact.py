@@ -6,12 +6,19 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .linear import _p, _stream
+from .linear import _p, _require, _stream
 
 
-def _f32(t, name):
-    if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
-        raise _lib.C3CUError(-1, name, "expected a contiguous fp32 CUDA tensor")
+def _f32(t, name, ndim: int = 2, shape=None):
+    _require(t, name, torch.float32, ndim, shape)
+
+
+def _bias(b, name: str):
+    """Bias of the fp32 kernels: any contiguous fp32 vector of at least one element (read as
+    bias[j] or bias[idx % numel], the reference's broadcast)."""
+    _f32(b, name, 1)
+    if b.numel() < 1:
+        raise _lib.C3CUError(-1, name, "a bias needs at least one element")
 
 
 def matmul(A: torch.Tensor, B: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
@@ -21,6 +28,11 @@ def matmul(A: torch.Tensor, B: torch.Tensor, trans_a: bool = False, trans_b: boo
     _f32(B, "B")
     M, K = (A.shape[1], A.shape[0]) if trans_a else (A.shape[0], A.shape[1])
     N = B.shape[0] if trans_b else B.shape[1]
+    _f32(B, "B", 2, (N, K) if trans_b else (K, N))
+    if bias is not None:
+        _bias(bias, "bias")
+        if bias.numel() not in (1, N):
+            raise _lib.C3CUError(-1, "bias", f"a matmul bias holds 1 or N={N} elements, got {bias.numel()}")
     out = torch.empty((M, N), dtype=torch.float32, device=A.device)
     rc = _lib.load().c3cu_matmul_f32(_p(A), _p(B), _p(out), M, K, N, int(trans_a), int(trans_b), _p(bias),
                                      0 if bias is None else bias.numel(), act, _stream(A.device))
@@ -33,9 +45,10 @@ def region_forward(X: torch.Tensor, B: torch.Tensor, b: torch.Tensor, trans_b: b
     """(out, z, mask) of the fp32 region: z = X B + b[idx % numel(b)], out = max(z, 0)."""
     _f32(X, "X")
     _f32(B, "B")
-    _f32(b, "b")
+    _bias(b, "b")
     M, K = X.shape
     N = B.shape[0] if trans_b else B.shape[1]
+    _f32(B, "B", 2, (N, K) if trans_b else (K, N))
     out = torch.empty((M, N), dtype=torch.float32, device=X.device)
     z = torch.empty_like(out) if want_z else None
     mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=X.device)

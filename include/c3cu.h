@@ -102,7 +102,9 @@ int c3cu_relu_mask_db(const void* dY, const uint32_t* mask, void* dZ, float* db,
  * c3cu_relu_mask_db_workspace(M, N) <= C3CU_NOALLOC_SCRATCH_BYTES (for N = 4096 up to
  * M = 130560 rows) and returns C3CU_ERR_WORKSPACE beyond that. It allocates nothing. Its
  * first call on a device looks up the array's device address, so make that first call
- * before any stream capture. All calls share the one array: calls that overlap on the GPU
+ * before any stream capture; after a cudaDeviceReset the next call looks it up again (the
+ * reloaded library's array may sit elsewhere), so make that call outside a capture too.
+ * M = 0 writes db = 0. All calls share the one array: calls that overlap on the GPU
  * (concurrent streams, or several host threads) race and must be serialised by the caller. */
 #define C3CU_NOALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
 int c3cu_relu_mask_db_noalloc(const void* dY, const uint32_t* mask, void* dZ, float* db,

@@ -61,7 +61,8 @@ def _no_alloc(L, dY, mask, stream):
     return dZ, db
 
 
-@pytest.mark.parametrize("M,N", [(16384, 4096), (1000, 300)])
+# cfg3's shape, a ragged shape, and the largest size the 4 MiB array holds at N = 4096
+@pytest.mark.parametrize("M,N", [(16384, 4096), (1000, 300), (130560, 4096)])
 def test_no_alloc_matches_workspace_entry_point_twice(cuda_device, M, N):
     L = _abi()
     stream = torch.cuda.current_stream(cuda_device).cuda_stream
@@ -78,9 +79,24 @@ def test_no_alloc_matches_workspace_entry_point_twice(cuda_device, M, N):
         assert bool(((db - db_ref).abs() <= bound).all())
 
 
+def test_no_alloc_empty_batch_writes_zero_db(cuda_device):
+    """M = 0 is an empty reduction: every column of db is +0, whatever db held before."""
+    L = _abi()
+    N = 300
+    db = torch.full((N,), float("nan"), dtype=torch.float32, device=cuda_device)
+    dummy = torch.empty(16, dtype=torch.uint8, device=cuda_device)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    rc = L.c3cu_relu_mask_db_noalloc(dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), db.data_ptr(),
+                                     0, N, stream)
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert bool((db == 0).all()) and not bool(torch.signbit(db).any())
+
+
 def test_no_alloc_refuses_sizes_beyond_its_array(cuda_device):
     L = _abi()
-    M, N = 130561, 4096  # one 512-row block more than the 4 MiB array holds at N = 4096
+    M, N = 130561, 4096  # one row more than the 4 MiB array holds at N = 4096
+    assert L.c3cu_relu_mask_db_workspace(M - 1, N) <= 4 * 1024 * 1024
     assert L.c3cu_relu_mask_db_workspace(M, N) > 4 * 1024 * 1024
     rc = L.c3cu_relu_mask_db_noalloc(None, None, None, None, M, N, None)
     assert rc == -6  # C3CU_ERR_WORKSPACE, refused before anything is launched
