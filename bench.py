@@ -6,8 +6,12 @@ Y = relu(X W^T + b) at global batch M=16384, N=K=4096, bf16 operands, fp32 accum
   forward  Y, mask = c3cu_linear_bias_relu_fwd(X, W, b)
   backward dZ, db  = c3cu_relu_mask_db(dY, mask); dW = dZ^T X; dX = dZ W
   N > 1    rows of X / dY are sharded across ranks (strong scaling at fixed global batch);
-           the packed [dW | db] fp32 buffer is summed by an NCCL all-reduce on a separate
-           stream, overlapped with the dX GEMM.
+           dW (bf16) and db (fp32) are summed by the library's in-switch all-reduce on a
+           separate stream, overlapped with the dX GEMM, and checked after the timed region
+           against an NCCL all-reduce of each rank's partials (allreduce_check).
+  N = 1    after the headline, the other BASELINE configs are measured in the same process
+           (configs: cfg2 forward, cfg4 chain, cfg5 FlashAttention, cfg1 MLP step), each with
+           its roofline fraction, a CPU baseline and a sampled parity check against the oracle.
 Metric: whole-job TFLOP/s = 3 * 2 * M * N * K / step time (max over ranks, CUDA events).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl c3|reference]
@@ -53,14 +57,19 @@ def _traffic():
 
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML during the timed region."""
+    """Samples the SM clock, the clock-event (throttle) reasons and the instantaneous power
+    through NVML every `interval` seconds (0.5 ms by default) during the timed region. A sample
+    counts as under load unless NVML flags the GPU idle (clock-event reason gpu_idle); the
+    reported clock is the median of the samples under load."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, index: int):
-        self.samples, self.reasons, self.max_mhz = [], set(), None
+    def __init__(self, index: int, interval: float = 0.0005):
+        self.samples = []  # (sm_mhz, reason bits, power_w or None)
+        self.max_mhz = None
+        self.interval = interval
         self._stop = threading.Event()
         self._t = None
         try:
@@ -72,18 +81,26 @@ class ClockSampler:
         except Exception:  # no NVML: the line carries no clock record
             self._nv = None
 
+    def _power_w(self):
+        nv = self._nv
+        try:
+            v = nv.nvmlDeviceGetFieldValues(self._h, [nv.NVML_FI_DEV_POWER_INSTANT])[0]
+            if v.nvmlReturn == 0:
+                return v.value.uiVal / 1000.0
+        except Exception:
+            pass
+        return None
+
     def _run(self):
         nv = self._nv
         while not self._stop.is_set():
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
                 bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                for b, name in self.REASONS.items():
-                    if bits & b:
-                        self.reasons.add(name)
+                self.samples.append((mhz, bits, self._power_w()))
             except Exception:
                 pass
-            self._stop.wait(0.01)
+            self._stop.wait(self.interval)
 
     def __enter__(self):
         if self._nv is not None:
@@ -99,8 +116,19 @@ class ClockSampler:
     def record(self):
         if self._nv is None or not self.samples:
             return None
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+        busy = [s for s in self.samples if not s[1] & 0x1]
+        use = busy or self.samples
+        reasons = set()
+        for _, bits, _ in use:
+            reasons |= {name for b, name in self.REASONS.items() if bits & b}
+        power = [p for _, _, p in use if p is not None]
+        return {"sm_mhz": statistics.median(m for m, _, _ in use), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons - {"gpu_idle"}), "samples": len(self.samples),
+                "samples_under_load": len(busy), "interval_ms": self.interval * 1e3,
+                "sm_mhz_min_under_load": min(m for m, _, _ in use),
+                "power_w_median": statistics.median(power) if power else None,
+                "power_w_max": max(power) if power else None,
+                "load": "samples without NVML's gpu_idle clock-event reason"}
 
 
 def _dist_env():
@@ -299,11 +327,16 @@ def run_c3(args):
     peak = peak_sust if long_region else peak_burst
     traffic = _traffic()
 
+    # ------------------------------------------------------------------ correctness at N > 1
+    ar_check = allreduce_check(train, X, W, b, dY, world) if world > 1 else None
+
     # ------------------------------------------------------------------ e2e (host buffers)
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, dev, world, rank, comp, X, W, b, dY)
 
+    clocks = sampler.record()
+    line = {}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -333,18 +366,44 @@ def run_c3(args):
                          "frac_of_spec_2250": achieved / 2250.0,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None},
             "gpu_launches": (4 + (chunks - 1) + (chunks if collective == "nvls" else 0)) * args.steps,
-            "clocks": sampler.record(),
+            "clocks": clocks,
         }
+        if clocks is not None:
+            # device time x median SM clock under load: the cycles each GEMM took, to read the
+            # roofline fraction against the clock the kernels ran at
+            line["kernel_kcycles"] = {k: ktime[k] * clocks["sm_mhz"] for k in ("fwd", "dw", "dx")}
+        if world > 1:
+            phases = {k: ktime[k] for k in kinds}
+            exposed = max(0.0, ms_per_step - sum(phases.values()))
+            phases["allreduce_exposed"] = exposed
+            line["critical_path"] = {"ms": phases, "limiting": max(phases, key=phases.get),
+                                     "allreduce_total_ms": ktime.get("allreduce")}
+            line["allreduce_check"] = ar_check
         if e2e is not None:
             line["e2e"] = e2e
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+        if world == 1 and not args.no_configs:
+            line["configs"] = run_configs(dev, peak_burst, hbm, line.get("cpu_baseline", {}).get("cores")
+                                          or _host_threads(), line.get("cpu_baseline"))
         print(json.dumps(line), flush=True)
     train.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    bad = (ar_check is not None and not ar_check["ok"])
+    if rank == 0 and "configs" in line:
+        bad = bad or not all(c["parity"]["ok"] for c in line["configs"].values())
+    if bad:
+        print("error: a correctness check in the benchmark failed (see allreduce_check / configs.*.parity)",
+              file=sys.stderr)
+        return 1
     return 0
+
+
+def _host_threads() -> int:
+    import oracle
+    return oracle.default_threads()
 
 
 def run_e2e(args, dev, world, rank, comp, X, W, b, dY):
@@ -439,6 +498,235 @@ def run_e2e(args, dev, world, rank, comp, X, W, b, dY):
                     "pipelined across steps on three streams (two device buffer sets)"}
 
 
+# --------------------------------------------------------------------------- multi-GPU check
+def allreduce_check(train, X, W, b, dY, world):
+    """After the timed region at N > 1: one more step leaves the summed dW / db in `train`; this
+    rank's partials are recomputed into private buffers and summed by torch.distributed (NCCL,
+    fp32) as the reference sum. dW must agree within one bf16 ulp of that sum (the in-switch
+    all-reduce adds the bf16 partials in fp32 and rounds once; NCCL's bf16 ring may round at
+    each of its world - 1 hops), db within 1e-5 of the sum of |terms| of its column. Returns the
+    record every rank computes (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from c3_b200 import linear
+    train(X, W, b, dY)
+    torch.cuda.synchronize()
+    dW_sum = train.dW.float()
+    db_sum = train.db.clone()
+    n, k, m = train.n, train.k, train.m
+    part = torch.empty_like(train.dW)
+    linear.gemm(train.dZ, X, True, True, train.epi, part, M=n, N=k, K=m)
+    dZ = torch.empty_like(train.dZ)
+    db_part = torch.empty(n, dtype=torch.float32, device=X.device)
+    linear.relu_mask_db(dY, train.mask, dZ, db_part)
+    ref = part.float()
+    dist.all_reduce(ref)
+    dist.all_reduce(db_part)
+    abs_terms = dZ.float().abs().sum(0)
+    dist.all_reduce(abs_terms)
+    if train.dW.dtype == torch.bfloat16:
+        e = torch.floor(torch.log2(ref.abs().clamp_min(2.0 ** -126)))
+        ulp = torch.exp2(e - 7)
+        dw_err = float(((dW_sum - ref).abs() / ulp).max())
+        tol = 1.0 if train.sync.collective == "nvls" else float(max(1, world - 1))
+        dw_key = "max_ulp"
+    else:
+        dw_err = float(((dW_sum - ref).abs() / ref.abs().max().clamp_min(1e-30)).max())
+        tol = 1e-5
+        dw_key = "max_rel"
+    db_err = float(((db_sum - db_part).abs() / (abs_terms + 1e-30)).max())
+    t = torch.tensor([dw_err, db_err], dtype=torch.float64, device=X.device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dw_err, db_err = float(t[0]), float(t[1])
+    ok = dw_err <= tol and db_err <= 1e-5
+    return {dw_key: dw_err, "tol": tol, "db_max_rel_to_abs_terms": db_err, "db_tol": 1e-5,
+            "against": "torch.distributed all_reduce (NCCL, fp32) of each rank's recomputed partials",
+            "collective": train.sync.collective, "ok": bool(ok)}
+
+
+# --------------------------------------------------------------------------- other configs
+def _timed(fn, iters, flush=None, stream=None):
+    """Mean device time (ms) of fn over `iters` launches, each bracketed by CUDA events on the
+    launching stream; `flush` (outside the events) evicts L2 between launches."""
+    import torch
+    st = stream or torch.cuda.current_stream()
+    pairs = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        pairs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in pairs) / iters
+
+
+def _bf16_grid(a):
+    import numpy as np
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return ((u + 0x7fff + ((u >> 16) & 1)) & 0xffff0000).view(np.float32)
+
+
+def run_configs(dev, peak_burst, hbm, cpu_cores, cpu_fwd=None):
+    """BASELINE's other configurations, measured in the same process after the headline (1 GPU):
+    each with its value, roofline fraction against MEASURED_PEAKS, a CPU baseline from the
+    oracle on a stated sample, and a sampled parity check against the oracle (tolerances of
+    tests/helpers.py: bf16 tensor-core paths 2e-2 normwise, fp32 paths 1e-5)."""
+    import math
+    import numpy as np
+    import torch
+    import oracle
+    from c3_b200 import elementwise, linear, mlp
+    from c3_b200.attention import flash_attn_fwd
+    out = {}
+    threads = cpu_cores
+    # the cfg2 CPU baseline is the headline's: the oracle's forward region on sampled rows
+    cpu_fwd = cpu_fwd or cpu_baseline()
+    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)
+
+    # ---- cfg2: fused Linear+bias+ReLU forward, X[8192,4096] x W^T[4096,4096] + b, bf16
+    M, N, K = 8192, 4096, 4096
+    g = torch.Generator(device=dev).manual_seed(2)
+    X = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    W = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b = torch.randn((N,), generator=g, device=dev) * 0.01
+    Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    mask = torch.empty((M, (N + 31) // 32), dtype=torch.int32, device=dev)
+    fwd = lambda: linear.forward(X, W, b, "nk", Y, mask)
+    for _ in range(3):
+        fwd()
+    ms = _timed(fwd, 20, flush)
+    flop = 2.0 * M * N * K
+    tf = flop / (ms * 1e-3) / 1e12
+    rows = np.linspace(0, M - 1, 32).astype(np.int64)
+    Xr = X[rows].float().cpu().numpy()
+    y_ref, _ = oracle.region_fwd(Xr, W.float().cpu().numpy(), b.cpu().numpy(), transB=True, threads=threads)
+    y = Y[rows].float().cpu().numpy()
+    err = float(np.abs(y - y_ref).max() / np.abs(y_ref).max())
+    words = mask.cpu().numpy().view(np.uint32)
+    bits = ((words[:, :, None] >> np.arange(32, dtype=np.uint32)) & 1).reshape(M, -1)[:, :N].astype(bool)
+    mask_ok = bool(np.array_equal(bits, (Y > 0).cpu().numpy()))
+    out["cfg2_fused_fwd"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": ms, "shape": {"M": M, "N": N, "K": K}, "dtype": "bf16",
+        "l2": "flushed between launches (256 MiB write outside the timed events)",
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_burst, "unit": "TFLOP/s",
+                     "frac": tf / peak_burst, "peak_kind": "measured burst"},
+        "cpu_baseline": cpu_fwd,
+        "parity": {"rows_checked": len(rows), "max_rel": err, "tol": 2e-2, "mask_matches_Y_gt_0": mask_ok,
+                   "ok": bool(err <= 2e-2 and mask_ok)}}
+    del X, W, b, Y, mask, Xr
+
+    # ---- cfg4: elementwise chain over 2^28 fp32 elements
+    n = 1 << 28
+    A = torch.rand(n, generator=g, device=dev) * 8 - 4
+    B = torch.rand(n, generator=g, device=dev) * 16 - 8
+    C = torch.rand(n, generator=g, device=dev) * 8 - 4
+    O = torch.empty_like(A)
+    chain = lambda: elementwise.chain_cfg4(A, B, C, O)
+    for _ in range(3):
+        chain()
+    ms = _timed(chain, 10)
+    gbs = 16.0 * n / (ms * 1e-3) / 1e9
+    sl = slice(n // 3, n // 3 + (1 << 20))
+    a_, b_, c_ = (t[sl].cpu().numpy() for t in (A, B, C))
+    ref = oracle.ew_cfg4(a_, b_, c_, threads=threads)
+    e4 = float(np.abs(O[sl].cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0))
+    cn = 1 << 24
+    a_, b_, c_ = (t[:cn].cpu().numpy() for t in (A, B, C))
+    t0 = time.perf_counter()
+    oracle.ew_cfg4(a_, b_, c_, threads=threads)
+    cpu_dt = time.perf_counter() - t0
+    out["cfg4_ew_chain"] = {
+        "value": gbs, "unit": "GB/s", "ms": ms, "elements": n, "dtype": "f32",
+        "l2": "inputs larger than L2 (3 x 1 GiB in, 1 GiB out)",
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_kind": "measured copy"},
+        "cpu_baseline": {"value": 16.0 * cn / cpu_dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{cn} of {n} elements (oracle, libm expf)"},
+        "parity": {"elements_checked": 1 << 20, "max_rel": e4, "tol": 1e-5, "ok": bool(e4 <= 1e-5)}}
+    del A, B, C, O
+
+    # ---- cfg5: causal FlashAttention forward, B8 H32 S8192 D128 bf16
+    Bt, H, S, D = 8, 32, 8192, 128
+    Q, Kt, V = (torch.randn((Bt, H, S, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    Oa = torch.empty_like(Q)
+    lse = torch.empty((Bt, H, S), dtype=torch.float32, device=dev)
+    att = lambda: flash_attn_fwd(Q, Kt, V, causal=True, out=Oa, lse=lse)
+    for _ in range(3):
+        att()
+    ms = _timed(att, 5)
+    flop = 2.0 * Bt * H * S * S * D  # causal: half of 4 B H S^2 D
+    tf = flop / (ms * 1e-3) / 1e12
+    worst = 0.0
+    lse_err = 0.0
+    scale = 1.0 / math.sqrt(D)
+    for (bb, hh, r0) in ((0, 0, 0), (3, 17, S - 64), (7, 31, S // 2)):
+        q, kk, vv = (t[bb, hh].float().cpu().numpy() for t in (Q, Kt, V))
+        o_ref, l_ref = oracle.attention_rows(q, kk, vv, scale, True, rows=(r0, r0 + 64))
+        o = Oa[bb, hh, r0:r0 + 64].float().cpu().numpy()
+        worst = max(worst, float(np.abs(o - o_ref).max() / np.abs(o_ref).max()))
+        lse_err = max(lse_err, float(np.abs(lse[bb, hh, r0:r0 + 64].cpu().numpy() - l_ref).max()))
+    t0 = time.perf_counter()
+    oracle.attention_rows(q, kk, vv, scale, True, rows=(S - 16, S))
+    cpu_dt = time.perf_counter() - t0
+    cpu_flop = 4.0 * D * sum(r + 1 for r in range(S - 16, S))
+    out["cfg5_flash_attn_fwd"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": ms, "shape": {"B": Bt, "H": H, "S": S, "D": D, "causal": True},
+        "dtype": "bf16", "l2": "inputs larger than L2 (Q, K, V 512 MiB each)",
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_burst, "unit": "TFLOP/s",
+                     "frac": tf / peak_burst, "peak_kind": "measured burst"},
+        "cpu_baseline": {"value": cpu_flop / cpu_dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                         "sample": "16 query rows at the end of one (batch, head), textbook attention "
+                                   "(no reference kernel exists)"},
+        "parity": {"rows_checked": 3 * 64, "max_rel": worst, "tol": 2e-2, "lse_max_abs": lse_err,
+                   "lse_tol": 2e-3, "ok": bool(worst <= 2e-2 and lse_err <= 2e-3)}}
+    del Q, Kt, V, Oa, lse
+
+    # ---- cfg1: MLP training step (fp32, bit-exact kernels), replayed from a CUDA graph
+    params = mlp.init_params(1234, dev)
+    ref_p = {k: v.cpu().numpy().copy() for k, v in params.items()}
+    x, y = mlp.synthetic_batch(100, 128, dev)
+    step = mlp.MLPTrainStep(params, batch=128, lr=0.01)
+    loss = float(step.step(x, y).item())
+    r_loss, r_logits, _, r_new = oracle.mlp_train_step(ref_p, x.cpu().numpy(), y.cpu().numpy(), 0.01)
+    logits_exact = bool(np.array_equal(step.z3.cpu().numpy(), r_logits))
+    perr = max(float(np.abs(params[k].cpu().numpy() - r_new[k]).max() / max(np.abs(r_new[k]).max(), 1e-30))
+               for k in mlp.PARAM_NAMES)
+    loss_err = abs(loss - r_loss) / abs(r_loss)
+    step.capture()
+    step.x_static.copy_(x)
+    step.y_static.copy_(y)
+    for _ in range(10):
+        step.replay()
+    graph_ms = _timed(step.replay, 200)
+    eager_ms = _timed(lambda: step.step(x, y), 50)
+    xs, ys = x.cpu().numpy(), y.cpu().numpy()
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        oracle.mlp_train_step(ref_p, xs, ys, 0.01)
+    cpu_us = (time.perf_counter() - t0) / reps * 1e6
+    flop_step = 2 * 128 * (784 * 256 + 256 * 128 + 128 * 10) * 2 + 2 * 128 * (256 * 128 + 128 * 10)
+    out["cfg1_mlp_step"] = {
+        "value": graph_ms * 1e3, "unit": "us/step", "higher_is_better": False, "eager_us": eager_ms * 1e3,
+        "batch": 128, "layers": [784, 256, 128, 10], "dtype": "f32 (bit-exact kernels)",
+        "launches_per_step": 15, "path": "c3_b200.mlp.MLPTrainStep over the C ABI, one CUDA graph per step",
+        "roofline": {"bound": "latency", "achieved": flop_step / (graph_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                     "peak": None, "frac": None,
+                     "note": "15 dependent launches of <= 10 us each; no HBM or tensor bound applies"},
+        "cpu_baseline": {"value": cpu_us, "unit": "us/step", "cores": 1, "kind": "port",
+                         "sample": f"{reps} x the whole step (oracle composition, one thread, as the reference's "
+                                   "serial matmul path)"},
+        "parity": {"logits_bit_exact": logits_exact, "loss_rel": loss_err, "params_max_rel": perr, "tol": 1e-5,
+                   "ok": bool(logits_exact and loss_err <= 1e-5 and perr <= 1e-5)}}
+    del flush_buf
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,6 +735,8 @@ def main():
     ap.add_argument("--impl", choices=["c3", "reference"], default="c3")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the in-run measurements of the other BASELINE configs (N=1)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
