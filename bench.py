@@ -6,9 +6,10 @@ Y = relu(X W^T + b) at global batch M=16384, N=K=4096, bf16 operands, fp32 accum
   forward  Y, mask = c3cu_linear_bias_relu_fwd(X, W, b)
   backward dZ, db  = c3cu_relu_mask_db(dY, mask); dW = dZ^T X; dX = dZ W
   N > 1    rows of X / dY are sharded across ranks (strong scaling at fixed global batch);
-           dW (bf16) and db (fp32) are summed by the library's in-switch all-reduce on a
-           separate stream, overlapped with the dX GEMM, and checked after the timed region
-           against an NCCL all-reduce of each rank's partials (allreduce_check).
+           dW (bf16) and db (fp32) are summed over the ranks by the dW GEMM itself (each tile
+           reduced in the NVSwitch as soon as every rank has computed it; C3_ALLREDUCE=nvls
+           runs the separate in-switch all-reduce overlapped with dX instead), and checked after
+           the timed region against an NCCL all-reduce of each rank's partials (allreduce_check).
   N = 1    after the headline, the other BASELINE configs are measured in the same process
            (configs: cfg2 forward, cfg4 chain, cfg5 FlashAttention, cfg1 MLP step), each with
            its roofline fraction, a CPU baseline and a sampled parity check against the oracle.
@@ -255,9 +256,11 @@ def run_c3(args):
     # (fp32 accumulation for bf16), unless C3_ALLREDUCE=nccl (process-group all_reduce).
     grad_dtype = env_grad_dtype()
     grad_bf16 = grad_dtype == torch.bfloat16
-    ar_env = os.environ.get("C3_ALLREDUCE", "nvls")
-    if ar_env not in ("nvls", "nccl", "group"):
-        raise ValueError(f"C3_ALLREDUCE must be nvls, nccl or group, got {ar_env!r}")
+    ar_env = os.environ.get("C3_ALLREDUCE", "fused")
+    if ar_env not in ("fused", "nvls", "nccl", "group"):
+        raise ValueError(f"C3_ALLREDUCE must be fused, nvls, nccl or group, got {ar_env!r}")
+    if grad_dtype != torch.bfloat16 and ar_env == "fused":
+        ar_env = "nvls"  # the fused dW GEMM + all-reduce writes a bf16 dW
     # Data-parallel overlap: the dW GEMM runs in `chunks` row bands of dW; each band's
     # all-reduce starts on the comm stream as soon as its GEMM ends (the last band carries
     # db). `reserve` SMs are left to the collective while the dX GEMM overlaps it.
@@ -265,7 +268,7 @@ def run_c3(args):
     ar_ctas, ar_sms = default_overlap(world)
     reserve = int(os.environ.get("C3_BENCH_AR_SMS", str(ar_sms))) if world > 1 else 0
     train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
-                                collective="auto" if ar_env == "nvls" else ar_env,
+                                collective="auto" if world == 1 else ar_env,
                                 chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", str(ar_ctas))),
                                 reserve_sms=reserve)
     chunks = len(train.bands)
@@ -346,11 +349,15 @@ def run_c3(args):
                        "N": N, "K": K, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (X, dY 128 MiB each at N=1)",
                        "step": "fwd GEMM+bias+ReLU+mask, mask*dY+db, dW GEMM, dX GEMM"
-                               + (f", all-reduce of dW and db in {chunks} band(s), each started when its"
-                                  f" dW band ends, overlapped with the rest of dW and dX" if world > 1 else ""),
+                               + ((", dW GEMM fused with the sum of dW and db over the ranks" if collective == "fused"
+                                   else f", all-reduce of dW and db in {chunks} band(s), each started when its"
+                                        f" dW band ends, overlapped with the rest of dW and dX") if world > 1 else ""),
                        "grad_dtype": {"dW": "bf16" if grad_bf16 else "fp32", "db": "fp32"},
                        "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
-                       "allreduce": {"nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce, "
+                       "allreduce": {"fused": "dW GEMM that sums dW and db over the ranks in its epilogue "
+                                              "(c3cu_gemm_dw_allreduce: each finished tile reduced in the "
+                                              "NVSwitch with multimem.ld_reduce/st while later tiles run)",
+                                     "nvls": "in-switch all-reduce kernel (c3cu_nvls_allreduce, "
                                              "multimem.ld_reduce/st) on torch symmetric memory",
                                      "nccl": "NCCL through c3cu_allreduce_grads",
                                      "group": "torch.distributed all_reduce (NCCL)",
@@ -528,7 +535,7 @@ def allreduce_check(train, X, W, b, dY, world):
         e = torch.floor(torch.log2(ref.abs().clamp_min(2.0 ** -126)))
         ulp = torch.exp2(e - 7)
         dw_err = float(((dW_sum - ref).abs() / ulp).max())
-        tol = 1.0 if train.sync.collective == "nvls" else float(max(1, world - 1))
+        tol = 1.0 if train.sync.collective in ("nvls", "fused") else float(max(1, world - 1))
         dw_key = "max_ulp"
     else:
         dw_err = float(((dW_sum - ref).abs() / ref.abs().max().clamp_min(1e-30)).max())

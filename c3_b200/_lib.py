@@ -65,6 +65,8 @@ _SIGNATURES = {
     "c3cu_nccl_comm_init": ([ctypes.POINTER(_vp), _vp, _i, _i], _i),
     "c3cu_nccl_comm_destroy": ([_vp], _i),
     "c3cu_allreduce_grads": ([_vp, _i64, _i, _vp, _vp], _i),
+    "c3cu_gemm_dw_allreduce": ([_vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i,
+                                ctypes.c_uint32, _vp], _i),
     "c3cu_nvls_allreduce_f32": ([_vp, _vp, _vp, _i64, _i64, _i, _i, ctypes.c_uint32, _i, _vp], _i),
     "c3cu_relu_mask_db_noalloc": ([_vp, _vp, _vp, _vp, _i64, _i64, _vp], _i),
     "c3cu_set_attn_variant": ([_i], _i),

@@ -24,8 +24,9 @@ def _align(n: int, a: int = 256) -> int:
 
 class NvlsAllReduce:
     def __init__(self, numel: int, device: torch.device, group=None, num_ctas: int = 32,
-                 numel_bf16: int = 0):
-        """numel fp32 elements (region `f32`) and numel_bf16 bf16 elements (region `bf16`)."""
+                 numel_bf16: int = 0, ar_flag_words: int = 0):
+        """numel fp32 elements (region `f32`) and numel_bf16 bf16 elements (region `bf16`), and
+        `ar_flag_words` uint32 counters for the fused dW GEMM + all-reduce (c3cu_gemm_dw_allreduce)."""
         import torch.distributed._symmetric_memory as symm_mem
         self.group = group or dist.group.WORLD
         self.numel = numel
@@ -36,7 +37,9 @@ class NvlsAllReduce:
         self.bf16_off = 0
         self.f32_off = _align(numel_bf16 * 2)
         self.flag_off = _align(self.f32_off + numel * 4)
-        nbytes = self.flag_off + 256
+        self.ar_flags_off = self.flag_off + 256
+        self.ar_flag_words = ar_flag_words
+        nbytes = self.ar_flags_off + _align(ar_flag_words * 4)
         self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
@@ -58,6 +61,9 @@ class NvlsAllReduce:
         self.mc = mc_base + offset
         self.flag_local = self.buf.data_ptr() + self.flag_off
         self.flag_mc = self.mc + self.flag_off
+        self.ar_flags_local = self.buf.data_ptr() + self.ar_flags_off
+        self.ar_flags_mc = self.mc + self.ar_flags_off
+        self.ar_epoch = 0
         self.f32 = self.buf[self.f32_off:self.f32_off + numel * 4].view(torch.float32)
         self.bf16 = self.buf[self.bf16_off:self.bf16_off + numel_bf16 * 2].view(torch.bfloat16)
         self.epoch = 0
@@ -93,6 +99,30 @@ class NvlsAllReduce:
                                              ctypes.c_void_p(s.cuda_stream))
         _lib.check(rc, "c3cu_nvls_allreduce")
         self.epoch += 1
+
+
+    def gemm_dw_allreduce_(self, dZ: torch.Tensor, X: torch.Tensor, n: int, k: int,
+                           stream: torch.cuda.Stream | None = None):
+        """dW = sum over ranks of dZ_r^T X_r into the bf16 region ([n, k], nn.Linear layout) and
+        db = the sum of the fp32 region's first n elements, in one launch of the fused dW GEMM
+        (c3cu_gemm_dw_allreduce). dZ [m, n] and X [m, k] are this rank's rows (bf16)."""
+        if self.ar_flag_words < 4 + 16 * ((n + 255) // 256) * ((k + 255) // 256):
+            raise ValueError("the buffer was made without enough flag words for this dW shape")
+        if self.numel_bf16 < n * k or self.numel < n:
+            raise ValueError("dW / db do not fit the buffer's regions")
+        m = dZ.shape[0]
+        if dZ.shape != (m, n) or X.shape != (m, k) or dZ.dtype != torch.bfloat16 or X.dtype != torch.bfloat16 \
+                or not dZ.is_contiguous() or not X.is_contiguous():
+            raise ValueError(f"expected contiguous bf16 dZ [{m}, {n}] and X [{m}, {k}]")
+        s = stream or torch.cuda.current_stream(self.buf.device)
+        rc = _lib.load().c3cu_gemm_dw_allreduce(
+            ctypes.c_void_p(dZ.data_ptr()), ctypes.c_void_p(X.data_ptr()),
+            ctypes.c_void_p(self.buf.data_ptr() + self.bf16_off), ctypes.c_void_p(self.mc + self.bf16_off),
+            ctypes.c_void_p(self.mc + self.f32_off), n, ctypes.c_void_p(self.ar_flags_local),
+            ctypes.c_void_p(self.ar_flags_mc), self.ar_flag_words, m, n, k, self.rank, self.world,
+            self.ar_epoch, ctypes.c_void_p(s.cuda_stream))
+        _lib.check(rc, "c3cu_gemm_dw_allreduce")
+        self.ar_epoch += 1
 
 
 class NcclComm:

@@ -276,6 +276,14 @@ int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ld
   p.partial = nullptr;
   p.tickets = nullptr;
   p.ready = nullptr;
+  p.ar_mc_out = nullptr;
+  p.ar_mc_db = nullptr;
+  p.ar_flags = nullptr;
+  p.ar_mc_flags = nullptr;
+  p.ar_db_count = 0;
+  p.ar_rank = 0;
+  p.ar_world = 1;
+  p.ar_epoch = 0u;
   const int esize = (epi == kEpiStoreF32 || epi == kEpiBiasStoreF32) ? 4 : 2;
   p.vec_ok = aligned16(out) && ((ldo * esize) % 16 == 0) &&
              (!bias_epi || aligned16(bias)) ? 1 : 0;
@@ -337,6 +345,73 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    int64_t ldm, int64_t M, int64_t N, int64_t K, c3cu_stream_t stream) {
   return c3cu::gemm_general(A, lda, a_mn, B, ldb, b_mn, out, ldo, epilogue, bias, mask, ldm, M,
                             N, K, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_gemm_dw_allreduce(const void* dZ, const void* X, void* dW, void* mc_dW, float* mc_db,
+                           int64_t db_count, uint32_t* flags, uint32_t* mc_flags, int64_t flag_words,
+                           int64_t M, int64_t N, int64_t K, int rank, int world, uint32_t epoch,
+                           c3cu_stream_t stream) {
+  using namespace c3cu;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // GEMM view: out dW[N][K] = dZ^T X, reduction over this rank's M rows; both operands MN-major
+  int rc = check_common(N, K, M);
+  if (rc != C3CU_OK) return rc;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || db_count < 0) {
+    set_error("gemm_dw_allreduce: bad rank %d / world %d / db_count %lld", rank, world, (long long)db_count);
+    return C3CU_ERR_INVALID;
+  }
+  if (N == 0 || K == 0) return C3CU_OK;
+  if (M == 0) {
+    set_error("gemm_dw_allreduce: a rank needs at least one row (M = 0)");
+    return C3CU_ERR_INVALID;
+  }
+  if (world == 1)  // nothing to sum: the plain dW GEMM
+    return gemm_general(dZ, N, 1, X, K, 1, dW, K, kEpiStoreBf16, nullptr, nullptr, 0, N, K, M, st);
+  if (!dZ || !X || !dW || !mc_dW || !flags || !mc_flags || (db_count > 0 && !mc_db)) {
+    set_error("gemm_dw_allreduce: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  if (!aligned16(dW) || !aligned16(mc_dW) || (K % 8) != 0 || (db_count % 4) != 0 ||
+      (db_count > 0 && !aligned16(mc_db)) || !aligned16(flags) || !aligned16(mc_flags)) {
+    set_error("gemm_dw_allreduce: dW, its multicast address, db and the flags must start on 16 bytes, "
+              "K must be a multiple of 8 and db_count of 4");
+    return C3CU_ERR_ALIGN;
+  }
+  if (N <= gemm2::HM) {
+    set_error("gemm_dw_allreduce: N = %lld rows of dW; the fused kernel runs on CTA pairs and needs N > %d",
+              (long long)N, gemm2::HM);
+    return C3CU_ERR_INVALID;
+  }
+  const int64_t tiles = ((N + gemm2::TM - 1) / gemm2::TM) * ((K + gemm2::TN - 1) / gemm2::TN);
+  if (flag_words < gemm2::ar::kRegion0 + gemm2::ar::kRegionsPerTile * tiles) {
+    set_error("gemm_dw_allreduce: %lld flag words, %lld needed", (long long)flag_words,
+              (long long)(gemm2::ar::kRegion0 + gemm2::ar::kRegionsPerTile * tiles));
+    return C3CU_ERR_INVALID;
+  }
+  gemm::Params p;
+  p.M = static_cast<int32_t>(N);
+  p.N = static_cast<int32_t>(K);
+  p.K = static_cast<int32_t>(M);
+  p.out = dW;
+  p.ldo = K;
+  p.bias = nullptr;
+  p.mask = nullptr;
+  p.ldm = 0;
+  p.vec_ok = 1;
+  p.sk_mode = 0;
+  p.sk_first = 0;
+  p.partial = nullptr;
+  p.tickets = nullptr;
+  p.ready = nullptr;
+  p.ar_mc_out = mc_dW;
+  p.ar_mc_db = mc_db;
+  p.ar_flags = flags;
+  p.ar_mc_flags = mc_flags;
+  p.ar_db_count = static_cast<int32_t>(db_count);
+  p.ar_rank = rank;
+  p.ar_world = world;
+  p.ar_epoch = epoch;
+  return launch_pair<true, true, kEpiBf16Allreduce>(dZ, N, X, K, p, st, 0);
 }
 
 int c3cu_linear_bias_relu_fwd(const void* X, const void* W, const float* bias, void* Y,

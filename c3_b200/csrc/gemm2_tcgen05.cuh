@@ -27,6 +27,7 @@
 
 #include "gemm2_schedule.h"
 #include "gemm_tcgen05.cuh"
+#include "multimem.cuh"
 
 namespace c3cu {
 namespace gemm2 {
@@ -94,6 +95,115 @@ __device__ __forceinline__ bool wait_ready(const uint32_t* flag) {
     }
   }
 }
+
+// ---------------------------------------------------------------- fused all-reduce epilogue
+// kEpiBf16Allreduce: the data-parallel dW GEMM sums its output over the ranks while it runs.
+// Every rank computes the same tiles in the same order (its own partial dW, from its rows of
+// the batch). An epilogue warp owns a region of 32 rows x 128 columns of a tile; after storing
+// its bf16 partial there it adds 1 to the region's counter in every rank's copy
+// (multimem.red.release). Once the counter shows all ranks, rank r's warp reduces slice r of
+// the region through the NVSwitch (multimem.ld_reduce with fp32 accumulation) and writes the
+// sum into every rank's copy (multimem.st). The reduction of a region is deferred by one tile,
+// so the ranks' progress on it has a tile's time to line up. db (fp32, already summed locally
+// by the pre-pass) is reduced the same way by the first CTA before its first tile.
+// Completion: each CTA takes a local ticket after its reductions; the last CTA of a rank adds 1
+// to the completion counter of every rank and waits until all ranks have arrived, so when the
+// kernel ends on a rank, dW and db hold the sums everywhere. Only that CTA waits at the end,
+// so CTAs of one grid never wait for one another. Counters only grow: launch e (the same on
+// every rank) waits for world * (e + 1). Every wait is bounded.
+namespace ar {
+constexpr int kDbFlag = 0;      // db: ranks whose pre-pass output is ready
+constexpr int kDoneFlag = 1;    // ranks whose reductions are all issued
+constexpr int kTicket = 2;      // this rank's CTAs that finished (local; zero between launches)
+constexpr int kRegion0 = 4;     // then 16 counters per output tile
+constexpr int kRegionsPerTile = 16;
+constexpr uint64_t kWaitNs = C3CU_WAIT_LIMIT_NS / 2;
+
+__device__ __forceinline__ uint32_t target(const gemm::Params& p) {
+  return static_cast<uint32_t>(p.ar_world) * (p.ar_epoch + 1u);
+}
+
+// After the warp's stores to its region: make them visible system-wide, then count the region.
+__device__ __forceinline__ void signal_region(const gemm::Params& p, uint32_t region, uint32_t lane) {
+  __syncwarp();
+  if (lane == 0) {
+    mm::fence_sys();
+    mm::red_release_add(p.ar_mc_flags + kRegion0 + region, 1u);
+  }
+  __syncwarp();
+}
+
+// This rank's slice of the region (rows row0.., columns col0..col0+127) once every rank stored
+// it: 512 16-byte vectors, slice r of world, up to 8 switch round trips in flight per lane.
+__device__ __forceinline__ void reduce_region(const gemm::Params& p, uint32_t region, int row0, int col0,
+                                              uint32_t lane) {
+  uint32_t ok = 1u;
+  if (lane == 0) ok = mm::wait_counter(p.ar_flags + kRegion0 + region, target(p), kWaitNs, region) ? 1u : 0u;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return;
+  constexpr int kVecs = 32 * 16;
+  const int per = (kVecs + p.ar_world - 1) / p.ar_world;
+  const int v0 = p.ar_rank * per;
+  const int v1 = min(kVecs, v0 + per);
+  uint8_t* base = static_cast<uint8_t*>(p.ar_mc_out);
+  for (int vb = v0; vb < v1; vb += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int vi = vb + u * 32 + static_cast<int>(lane);
+      const int r = row0 + vi / 16;
+      const int c = col0 + (vi % 16) * 8;
+      if (vi < v1 && r < p.M && c < p.N) mm::ld_reduce_bf16x8(base + ((int64_t)r * p.ldo + c) * 2, v[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int vi = vb + u * 32 + static_cast<int>(lane);
+      const int r = row0 + vi / 16;
+      const int c = col0 + (vi % 16) * 8;
+      if (vi < v1 && r < p.M && c < p.N) mm::st_bf16x8(base + ((int64_t)r * p.ldo + c) * 2, v[u]);
+    }
+  }
+}
+
+// db: the first CTA's eight epilogue warps (thread t = 32 * warp + lane, 256 threads) sum this
+// rank's slice of db over the ranks, before their first tile.
+__device__ __forceinline__ void reduce_db(const gemm::Params& p, uint32_t ew, uint32_t lane) {
+  const int t = static_cast<int>(ew * 32u + lane);
+  if (t == 0) {
+    mm::fence_sys();
+    mm::red_release_add(p.ar_mc_flags + kDbFlag, 1u);
+  }
+  uint32_t ok = 1u;
+  if (lane == 0) ok = mm::wait_counter(p.ar_flags + kDbFlag, target(p), kWaitNs, 0xfffeu) ? 1u : 0u;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok || p.ar_db_count <= 0) return;
+  const int nvec = p.ar_db_count / 4;
+  const int per = (nvec + p.ar_world - 1) / p.ar_world;
+  const int v0 = p.ar_rank * per;
+  const int v1 = min(nvec, v0 + per);
+  for (int v = v0 + t; v < v1; v += 256) {
+    float4 x;
+    mm::ld_reduce_f32x4(p.ar_mc_db + 4 * v, x);
+    mm::st_f32x4(p.ar_mc_db + 4 * v, x);
+  }
+}
+
+// End of the epilogue of one CTA (all eight epilogue warps call it).
+__device__ __forceinline__ void finish(const gemm::Params& p, uint32_t ew, uint32_t lane) {
+  asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps' reductions are issued
+  if (ew == 0 && lane == 0) {
+    mm::fence_sys();
+    const uint32_t t = atomicAdd(p.ar_flags + kTicket, 1u);
+    if (t == gridDim.x - 1u) {
+      p.ar_flags[kTicket] = 0u;  // every CTA of this launch has taken its ticket
+      mm::fence_sys();
+      mm::red_release_add(p.ar_mc_flags + kDoneFlag, 1u);
+      mm::wait_counter(p.ar_flags + kDoneFlag, target(p), kWaitNs, 0xffffu);
+    }
+  }
+  __syncwarp();
+}
+}  // namespace ar
 
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -227,6 +337,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t ew = warp - 2u;                // epilogue warp 0..7
     const int c_lo = static_cast<int>(ew >> 2) * (TN / 64);  // first of this warp's 4 chunks
     uint32_t acc = 0, acc_ph = 0;
+    [[maybe_unused]] int pend_region = -1, pend_row = 0, pend_col = 0;
+    if constexpr (EPI == kEpiBf16Allreduce) {
+      if (blockIdx.x == 0) ar::reduce_db(p, ew, lane);
+    }
     Item it;
     for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it); ++i) {
       const int m0 = (it.tile / n_tiles) * TM + static_cast<int>(rank) * HM;
@@ -276,7 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j)
             r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __ldcg(part + (c * 32 + j) * HM)));
         }
-        gemm::epilogue_chunk<EPI>(p, r, row, col0);
+        gemm::epilogue_chunk<EPI == kEpiBf16Allreduce ? kEpiStoreBf16 : EPI>(p, r, row, col0);
       }
       if (split) {
         __threadfence();
@@ -296,6 +410,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0u));
       acc ^= 1u;
       if (acc == 0u) acc_ph ^= 1u;
+      if constexpr (EPI == kEpiBf16Allreduce) {
+        if (!split || adder) {  // this warp stored its region of the tile on this rank
+          const int region = it.tile * ar::kRegionsPerTile + static_cast<int>(rank * 8u + ew);
+          ar::signal_region(p, static_cast<uint32_t>(region), lane);
+          if (pend_region >= 0) ar::reduce_region(p, static_cast<uint32_t>(pend_region), pend_row, pend_col, lane);
+          pend_region = region;
+          pend_row = m0 + static_cast<int>(q * 32u);
+          pend_col = n0 + c_lo * 32;
+        }
+      }
+    }
+    if constexpr (EPI == kEpiBf16Allreduce) {
+      if (pend_region >= 0) ar::reduce_region(p, static_cast<uint32_t>(pend_region), pend_row, pend_col, lane);
+      ar::finish(p, ew, lane);
     }
   }
 

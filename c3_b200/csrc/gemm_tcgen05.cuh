@@ -30,6 +30,8 @@ enum Epilogue : int {
   kEpiStoreBf16 = 1,     // out bf16 = acc
   kEpiStoreF32 = 2,      // out f32  = acc
   kEpiBiasStoreF32 = 3,  // out f32  = acc + bias[n]
+  kEpiBf16Allreduce = 4, // out bf16 = acc, then summed over ranks in the NVSwitch (CTA-pair
+                         // kernel only; gemm2_tcgen05.cuh, namespace ar)
 };
 
 namespace gemm {
@@ -68,6 +70,18 @@ struct Params {
   float* partial;
   uint32_t* tickets;
   uint32_t* ready;
+  // kEpiBf16Allreduce: `out` is this rank's copy of a buffer bound to an NVLink multicast
+  // object and `ar_mc_out` its multicast address; `ar_mc_db` the multicast address of an fp32
+  // vector of `ar_db_count` elements summed alongside; `ar_flags` / `ar_mc_flags` this rank's
+  // copy and the multicast address of the flag words (monotonic counters, see gemm2 ar::).
+  void* ar_mc_out;
+  float* ar_mc_db;
+  uint32_t* ar_flags;
+  uint32_t* ar_mc_flags;
+  int32_t ar_db_count;
+  int32_t ar_rank;
+  int32_t ar_world;
+  uint32_t ar_epoch;
 };
 
 template <bool A_MN, bool B_MN>

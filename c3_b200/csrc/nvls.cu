@@ -17,6 +17,7 @@
 // No TMA and no multicast TMA loads are used; only multimem loads/stores/reductions.
 #include "common.cuh"
 #include "host_util.h"
+#include "multimem.cuh"
 
 C3CU_FAULT_ACCESSORS(nvls)
 
@@ -26,36 +27,14 @@ namespace nvls {
 constexpr int kThreads = 512;
 constexpr int kUnroll = 8;
 
-__device__ __forceinline__ void mm_ld_reduce_v4(const float* mc, float4& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(mc)
-               : "memory");
-}
-
-__device__ __forceinline__ void mm_st_v4(float* mc, const float4& v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x),
-               "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-
-__device__ __forceinline__ void mm_ld_reduce(const float* mc, float& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(mc) : "memory");
-}
-
-__device__ __forceinline__ void mm_st(float* mc, float v) {
-  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void mm_red_release_add(uint32_t* mc, uint32_t v) {
-  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+using mm::ld_acquire_sys;
+using mm::ld_reduce_bf16x8;
+using mm::ld_reduce_f32;
+using mm::ld_reduce_f32x4;
+using mm::red_release_add;
+using mm::st_bf16x8;
+using mm::st_f32;
+using mm::st_f32x4;
 
 // Grid-wide cross-rank barrier: every CTA adds 1 through the multicast address, then waits
 // until all world * gridDim.x arrivals of this phase are visible in the local copy.
@@ -64,7 +43,7 @@ __device__ bool barrier(uint32_t* mc_flag, const uint32_t* local_flag, uint32_t 
   bool ok = true;
   if (threadIdx.x == 0) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    mm_red_release_add(mc_flag, 1u);
+    red_release_add(mc_flag, 1u);
     const uint64_t t0 = globaltimer_ns();
     while (static_cast<int32_t>(ld_acquire_sys(local_flag) - target) < 0) {
       if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS / 2) {
@@ -76,19 +55,6 @@ __device__ bool barrier(uint32_t* mc_flag, const uint32_t* local_flag, uint32_t 
   }
   __syncthreads();
   return __syncthreads_and(ok ? 1 : 0) != 0;
-}
-
-__device__ __forceinline__ void mm_ld_reduce_bf16x8(const void* mc, uint4& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(mc)
-               : "memory");
-}
-
-__device__ __forceinline__ void mm_st_bf16x8(void* mc, const uint4& v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
-               "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
 }
 
 // Reduces this rank's slice of a segment of `count` elements at `mc` (16-byte units of
@@ -108,10 +74,10 @@ __device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int r
     for (int u = 0; u < kUnroll; ++u) {
       uint8_t* a = mc + (i + stride * u) * 16;
       if (BF16) {
-        mm_ld_reduce_bf16x8(a, v[u]);
+        ld_reduce_bf16x8(a, v[u]);
       } else {
         float4 f;
-        mm_ld_reduce_v4(reinterpret_cast<float*>(a), f);
+        ld_reduce_f32x4(reinterpret_cast<float*>(a), f);
         v[u] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
       }
     }
@@ -119,9 +85,9 @@ __device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int r
     for (int u = 0; u < kUnroll; ++u) {
       uint8_t* a = mc + (i + stride * u) * 16;
       if (BF16)
-        mm_st_bf16x8(a, v[u]);
+        st_bf16x8(a, v[u]);
       else
-        mm_st_v4(reinterpret_cast<float*>(a), make_float4(__uint_as_float(v[u].x), __uint_as_float(v[u].y),
+        st_f32x4(reinterpret_cast<float*>(a), make_float4(__uint_as_float(v[u].x), __uint_as_float(v[u].y),
                                                           __uint_as_float(v[u].z), __uint_as_float(v[u].w)));
     }
   }
@@ -129,12 +95,12 @@ __device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int r
     uint8_t* a = mc + i * 16;
     if (BF16) {
       uint4 v;
-      mm_ld_reduce_bf16x8(a, v);
-      mm_st_bf16x8(a, v);
+      ld_reduce_bf16x8(a, v);
+      st_bf16x8(a, v);
     } else {
       float4 f;
-      mm_ld_reduce_v4(reinterpret_cast<float*>(a), f);
-      mm_st_v4(reinterpret_cast<float*>(a), f);
+      ld_reduce_f32x4(reinterpret_cast<float*>(a), f);
+      st_f32x4(reinterpret_cast<float*>(a), f);
     }
   }
 }
@@ -174,26 +140,26 @@ __global__ void __launch_bounds__(kThreads)
       for (; i + 4 * stride * (kUnroll - 1) < v1; i += 4 * stride * kUnroll) {
         float4 v[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) mm_ld_reduce_v4(mc_data + i + 4 * stride * u, v[u]);
+        for (int u = 0; u < kUnroll; ++u) ld_reduce_f32x4(mc_data + i + 4 * stride * u, v[u]);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) mm_st_v4(mc_data + i + 4 * stride * u, v[u]);
+        for (int u = 0; u < kUnroll; ++u) st_f32x4(mc_data + i + 4 * stride * u, v[u]);
       }
       for (; i < v1; i += 4 * stride) {
         float4 v;
-        mm_ld_reduce_v4(mc_data + i, v);
-        mm_st_v4(mc_data + i, v);
+        ld_reduce_f32x4(mc_data + i, v);
+        st_f32x4(mc_data + i, v);
       }
     }
     // unaligned head and tail of the slice
     for (int64_t i = s0 + t; i < min(v0, s1); i += stride) {
       float v;
-      mm_ld_reduce(mc_data + i, v);
-      mm_st(mc_data + i, v);
+      ld_reduce_f32(mc_data + i, v);
+      st_f32(mc_data + i, v);
     }
     for (int64_t i = max(v1, v0) + t; i < s1; i += stride) {
       float v;
-      mm_ld_reduce(mc_data + i, v);
-      mm_st(mc_data + i, v);
+      ld_reduce_f32(mc_data + i, v);
+      st_f32(mc_data + i, v);
     }
   }
   barrier(mc_flag, local_flag, arrivals * (2u * epoch + 2u));

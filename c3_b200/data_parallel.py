@@ -14,7 +14,11 @@ bands of dW (`dw_bands`): each band's all-reduce starts on a communication strea
 its GEMM ends, overlapped with the remaining bands and with the dX GEMM.
 
 `GradientSync` owns one rank's dW / db and sums them:
-- "nvls": the library's in-switch all-reduce on NVLink-multicast memory (c3_b200.collective);
+- "fused" (default for a bf16 dW on GPUs): the dW GEMM itself sums dW and db over the ranks
+  (c3cu_gemm_dw_allreduce): each finished tile of dW is reduced in the NVSwitch while the
+  tensor cores work on the next ones, so the exchange needs no separate launch or stream;
+- "nvls": the library's in-switch all-reduce on NVLink-multicast memory (c3_b200.collective),
+  a separate kernel on a communication stream after the dW GEMM;
 - "nccl": NCCL through the library's C ABI (c3cu_allreduce_grads on a communicator made by
   c3cu_nccl_comm_init), as a C++ host calls it;
 - "group": torch.distributed all_reduce on the process group (NCCL for CUDA tensors, gloo for
@@ -88,8 +92,10 @@ class GradientSync:
                  collective: str = "auto", group=None, num_ctas: int = 16):
         if grad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError(f"dW dtype must be bfloat16 or float32, got {grad_dtype}")
-        if collective not in ("auto", "nvls", "nccl", "group"):
-            raise ValueError(f"collective must be 'auto', 'nvls', 'nccl' or 'group', got {collective!r}")
+        if collective not in ("auto", "fused", "nvls", "nccl", "group"):
+            raise ValueError(f"collective must be 'auto', 'fused', 'nvls', 'nccl' or 'group', got {collective!r}")
+        if collective == "fused" and grad_dtype != torch.bfloat16:
+            raise ValueError("the fused dW GEMM + all-reduce writes a bf16 dW")
         self.n, self.k = n, k
         self.device = torch.device(device)
         self.grad_dtype = grad_dtype
@@ -97,21 +103,25 @@ class GradientSync:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.nvls = None
         self.nccl = None
-        want_nvls = collective == "nvls" or (collective == "auto" and self.device.type == "cuda"
-                                             and self.world > 1)
+        want_nvls = collective in ("nvls", "fused") or (collective == "auto" and self.device.type == "cuda"
+                                                        and self.world > 1)
+        self.fused = False
         if want_nvls:
             try:
                 from .collective import NvlsAllReduce
                 if grad_dtype == torch.bfloat16:
+                    fused = collective in ("fused", "auto") and n > 128 and k % 8 == 0 and n % 4 == 0
+                    words = 4 + 16 * ((n + 255) // 256) * ((k + 255) // 256) if fused else 0
                     self.nvls = NvlsAllReduce(n, self.device, group=group, num_ctas=num_ctas,
-                                              numel_bf16=n * k)
+                                              numel_bf16=n * k, ar_flag_words=words)
+                    self.fused = fused
                     self.dW, self.db = self.nvls.bf16.view(n, k), self.nvls.f32
                 else:
                     self.nvls = NvlsAllReduce(n * k + n, self.device, group=group, num_ctas=num_ctas)
                     flat = self.nvls.data()
                     self.dW, self.db = flat[: n * k].view(n, k), flat[n * k:]
             except Exception as exc:
-                if collective == "nvls":
+                if collective in ("nvls", "fused"):
                     raise
                 print(f"warning: NVLS all-reduce unavailable ({exc}); using the process group",
                       file=sys.stderr)
@@ -119,7 +129,8 @@ class GradientSync:
         if collective == "nccl" and self.world > 1:
             from .collective import NcclComm
             self.nccl = NcclComm(self.device, group)
-        self.collective = "nvls" if self.nvls is not None else ("nccl" if self.nccl else "group")
+        self.collective = ("fused" if self.fused else "nvls") if self.nvls is not None else \
+            ("nccl" if self.nccl else "group")
         if self.nvls is None:
             if grad_dtype == torch.bfloat16:
                 self.dW = torch.empty((n, k), dtype=grad_dtype, device=self.device)
@@ -128,6 +139,10 @@ class GradientSync:
                 flat = torch.empty(n * k + n, dtype=torch.float32, device=self.device)
                 self.dW, self.db = flat[: n * k].view(n, k), flat[n * k:]
         self._flat_f32 = None if grad_dtype == torch.bfloat16 else flat
+
+    def gemm_dw_reduce_(self, dZ: torch.Tensor, X: torch.Tensor, stream=None):
+        """The fused path: dW = sum over ranks of dZ_rᵀ X_r and db summed in place, one launch."""
+        self.nvls.gemm_dw_allreduce_(dZ, X, self.n, self.k, stream)
 
     def reduce_(self, rows: tuple[int, int] | None = None, with_db: bool = True, stream=None):
         """Sum dW rows [lo, hi) (all rows by default) and, with `with_db`, db over the group.
@@ -199,7 +214,8 @@ class LinearReluTrainStep:
 
     forward (Y bf16 + bit-packed ReLU mask) → pre-pass (dZ, db) → dW GEMM in bands, each band's
     all-reduce on `comm` → dX GEMM → the compute stream waits for the last all-reduce.
-    `reserve_sms` SMs are left to the collective while the dX GEMM overlaps it."""
+    `reserve_sms` SMs are left to the collective while the dX GEMM overlaps it. With the
+    "fused" collective: forward → pre-pass → dW GEMM that sums dW and db over the ranks → dX."""
 
     PHASES = ("fwd", "prepass", "dw", "dx")
 
@@ -211,7 +227,7 @@ class LinearReluTrainStep:
         self.device = torch.device(device)
         self.sync = GradientSync(n, k, self.device, grad_dtype, collective, group, num_ctas)
         self.world = self.sync.world
-        self.bands = dw_bands(n, chunks)
+        self.bands = [(0, n)] if self.sync.fused else dw_bands(n, chunks)
         self.reserve_sms = reserve_sms if self.world > 1 else 0
         self.epi = _lib.EPI_STORE_BF16 if grad_dtype == torch.bfloat16 else _lib.EPI_STORE_F32
         dev = self.device
@@ -251,6 +267,14 @@ class LinearReluTrainStep:
         mark("prepass"); linear.relu_mask_db(dY, self.mask, self.dZ, self.db); mark("prepass")
         mark("dw")
         m, k = self.m, self.k
+        if self.sync.fused:
+            # dW GEMM and the sum of dW and db over the ranks in one launch; dX follows alone
+            self.sync.gemm_dw_reduce_(self.dZ, X, comp)
+            mark("dw")
+            mark("dx"); linear.grad_input(self.dZ, W, "nk", self.dX); mark("dx")
+            if record:
+                return StepEvents({p: (phases[p][0], phases[p][1]) for p in self.PHASES}, ar)
+            return None
         for i, (r0, r1) in enumerate(self.bands):
             linear.gemm(self.dZ[:, r0:r1], X, True, True, self.epi, self.dW[r0:r1], M=r1 - r0, N=k, K=m)
             if self.world > 1:

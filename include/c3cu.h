@@ -242,6 +242,29 @@ int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, fl
  * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM. */
 int c3cu_set_attn_variant(int variant);
 
+/* ------------------------------------------------------------------ fused dW GEMM + all-reduce
+ * The data-parallel backward's exchange step fused into the dW GEMM that produces it (replaces
+ * the dW graph of MatMul backward, src/C3/C3BackwardCapture.cpp:681-723, followed by a sum over
+ * ranks; the reference runs one process and has no collective):
+ *   dW[N][K] = sum over ranks of dZ_r^T X_r   (bf16 out, fp32 accumulation, one rounding per
+ *                                              rank, fp32 accumulation of the ranks' partials
+ *                                              in the NVSwitch)
+ *   db[n]    = sum over ranks of db_r[n]       (fp32, in place)
+ * dZ_r [M][N] and X_r [M][K] are this rank's rows (M may differ per rank, M >= 1). dW is this
+ * rank's copy of a buffer that every rank bound to one NVLink multicast object, mc_dW its
+ * multicast address; mc_db the multicast address of this rank's db_r (db_count fp32, a multiple
+ * of 4; 0 for none); flags / mc_flags this rank's copy and the multicast address of
+ * C3CU_AR_FLAG_WORDS(N, K) uint32 words in multicast memory, zero before the first call. Every
+ * rank makes the same sequence of calls with epoch = 0, 1, 2, ... When the call completes on
+ * the stream, dW and db hold the sums on every rank. Each tile of dW is reduced as soon as all
+ * ranks have computed it, while later tiles are still on the tensor cores. Waits for other
+ * ranks are bounded (2 s) and record C3CU_ERR_FAULT. world == 1 runs the plain dW GEMM. */
+#define C3CU_AR_FLAG_WORDS(N, K) (4 + 16 * ((((N) + 255) / 256) * (((K) + 255) / 256)))
+int c3cu_gemm_dw_allreduce(const void* dZ, const void* X, void* dW, void* mc_dW, float* mc_db,
+                           int64_t db_count, uint32_t* flags, uint32_t* mc_flags, int64_t flag_words,
+                           int64_t M, int64_t N, int64_t K, int rank, int world, uint32_t epoch,
+                           c3cu_stream_t stream);
+
 /* ------------------------------------------------------------------ data-parallel collective
  * In-switch (NVLink SHARP) all-reduce (sum) of fp32 elements [lo, hi) of a buffer that every
  * rank has bound to one NVLink multicast object. mc_data / mc_flag are the multicast

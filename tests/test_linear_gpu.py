@@ -357,3 +357,29 @@ def test_prepass_on_two_streams_at_once(cuda_device):
         assert torch.equal(dz, r1[0]) and torch.equal(db, r1[1])
     for (dz, db) in outs2:
         assert torch.equal(dz, r2[0]) and torch.equal(db, r2[1])
+
+
+def test_fused_dw_allreduce_single_rank_is_the_dw_gemm(cuda_device):
+    """c3cu_gemm_dw_allreduce with world = 1 has nothing to sum: it is the bf16 dW GEMM (same
+    bits as grad_weight's), and it refuses a multi-rank call whose buffers are not set."""
+    import ctypes
+
+    from c3_b200 import _lib
+    L = _lib.load()
+    M, N, K = 640, 384, 520
+    dZ = randn((M, N), 1e-2, 41).to(cuda_device)
+    X = randn((M, K), 1.0, 42).to(cuda_device)
+    dW = torch.empty((N, K), dtype=torch.bfloat16, device=cuda_device)
+    s = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    rc = L.c3cu_gemm_dw_allreduce(ctypes.c_void_p(dZ.data_ptr()), ctypes.c_void_p(X.data_ptr()),
+                                  ctypes.c_void_p(dW.data_ptr()), None, None, 0, None, None, 0,
+                                  M, N, K, 0, 1, 0, s)
+    assert rc == 0, _lib.last_error()
+    ref = linear.grad_weight(dZ, X, "nk", out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(dW.view(torch.int16), ref.view(torch.int16))
+    assert_bf16_close(f32(dW), oracle.matmul(f32(dZ), f32(X), transA=True), "dW (world 1)")
+    rc = L.c3cu_gemm_dw_allreduce(ctypes.c_void_p(dZ.data_ptr()), ctypes.c_void_p(X.data_ptr()),
+                                  ctypes.c_void_p(dW.data_ptr()), None, None, 0, None, None, 0,
+                                  M, N, K, 0, 2, 0, s)
+    assert rc == -1 and "null" in _lib.last_error()

@@ -1,5 +1,6 @@
 """Data-parallel path on 2 GPUs (child processes, one per GPU): the in-switch all-reduce kernel
-against NCCL's all_reduce on the same buffers, the row-sharded training step against the
+against NCCL's all_reduce on the same buffers, the dW GEMM with the all-reduce fused into its
+epilogue against NCCL's sum of the same partials, the row-sharded training step against the
 one-GPU step on the full batch, and the data-parallel cfg1 MLP step (eager and CUDA-graph
 replay, one NCCL all-reduce of gradients + loss per step) against the one-GPU full-batch step.
 Skipped when fewer than 2 GPUs are visible."""
@@ -112,6 +113,83 @@ def test_nvls_allreduce_matches_nccl(cuda_device):
         assert all(v <= 1e-6 for v in res.values()), res
 
 
+def _fused_worker(rank, world, port, q):
+    """c3cu_gemm_dw_allreduce on `world` GPUs: dW = sum over ranks of dZ_rᵀ X_r (bf16) and db
+    summed in place, against torch.distributed's fp32 all_reduce of the same partials, over
+    several epochs with fresh data each call. Shapes: ragged (K not a multiple of the tile) and
+    one whose tiles run as split-K halves (fewer tiles than clusters, long reduction)."""
+    try:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        import c3_b200
+        from c3_b200 import _lib, linear
+        from c3_b200.collective import NvlsAllReduce
+        res = {}
+        for (m, n, k) in ((500, 512, 384), (4096, 1024, 1024), (300 + 37 * rank, 384, 1032)):
+            words = 4 + 16 * ((n + 255) // 256) * ((k + 255) // 256)
+            buf = NvlsAllReduce(n, dev, num_ctas=8, numel_bf16=n * k, ar_flag_words=words)
+            dW, db = buf.bf16.view(n, k), buf.f32
+            worst_ulp, worst_db = 0.0, 0.0
+            for epoch in range(3):
+                g = torch.Generator(device=dev).manual_seed(1000 * epoch + 17 * rank + m)
+                dZ = (torch.randn((m, n), generator=g, device=dev) * 1e-2).to(torch.bfloat16)
+                X = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+                db_part = torch.randn(n, generator=g, device=dev)
+                db.copy_(db_part)
+                dW.fill_(float("nan"))  # every element must be written by this call
+                torch.cuda.synchronize()
+                buf.gemm_dw_allreduce_(dZ, X, n, k)
+                part = linear.grad_weight(dZ, X, "nk", out_dtype=torch.bfloat16)
+                ref = part.float()
+                dist.all_reduce(ref)
+                ref_db = db_part.clone()
+                dist.all_reduce(ref_db)
+                absdb = db_part.abs()
+                dist.all_reduce(absdb)
+                torch.cuda.synchronize()
+                ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(2.0 ** -126))) - 7)
+                worst_ulp = max(worst_ulp, float(((dW.float() - ref).abs() / ulp).max()))
+                worst_db = max(worst_db, float(((db - ref_db).abs() / (absdb + 1e-30)).max()))
+            res[f"{m}x{n}x{k}_ulp"] = worst_ulp
+            res[f"{m}x{n}x{k}_db"] = worst_db
+            del buf
+        res["fault"] = c3_b200.fault_status()
+        q.put((rank, "ok", res))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc)))
+
+
+def test_fused_dw_allreduce_matches_nccl(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, res in out:
+        assert status == "ok", f"rank {rank}: {res}"
+        assert res["fault"] == 0, res
+        for key, v in res.items():
+            if key.endswith("_ulp"):  # fp32 sum in the switch, one conversion to bf16
+                assert v <= 1.0, (key, res)
+            elif key.endswith("_db"):
+                assert v <= 1e-6, (key, res)
+
+
 def _step_worker(rank, world, port, q):
     """The row-sharded training step (c3_b200.data_parallel.LinearReluTrainStep) on `world`
     GPUs against the one-GPU kernels on the full batch."""
@@ -135,7 +213,8 @@ def _step_worker(rank, world, port, q):
         dY = (torch.randn((M, N), generator=g, device=dev) * 1e-2).to(torch.bfloat16)
         lo, hi = shard_rows(M, world, rank)
         res = {}
-        for grad_dtype, chunks, coll in ((torch.bfloat16, 1, "nvls"), (torch.bfloat16, 4, "nvls"),
+        for grad_dtype, chunks, coll in ((torch.bfloat16, 1, "fused"), (torch.bfloat16, 1, "nvls"),
+                                         (torch.bfloat16, 4, "nvls"),
                                          (torch.float32, 2, "nvls"), (torch.bfloat16, 2, "nccl"),
                                          (torch.float32, 1, "nccl")):
             step = LinearReluTrainStep(hi - lo, N, K, dev, grad_dtype, collective=coll, chunks=chunks,
