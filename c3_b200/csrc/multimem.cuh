@@ -63,12 +63,15 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Bounded acquire-wait until this rank's copy of a monotonic counter reaches `target`
-// (wraparound-safe comparison). On time-out records kFaultWaitPeer with `site` and returns false.
+// (wraparound-safe comparison). On time-out records kFaultWaitPeer with `site` and returns false;
+// it also gives up at once when this unit's fault word is already set (a peer that missed one
+// counter would miss the later ones too, and each would otherwise wait out its own limit).
 __device__ __forceinline__ bool wait_counter(const uint32_t* local, uint32_t target, uint64_t limit_ns,
                                              uint32_t site) {
   if (static_cast<int32_t>(ld_acquire_sys(local) - target) >= 0) return true;
   const uint64_t t0 = globaltimer_ns();
   while (static_cast<int32_t>(ld_acquire_sys(local) - target) < 0) {
+    if (fault_raised()) return false;
     if (globaltimer_ns() - t0 > limit_ns) {
       record_fault(kFaultWaitPeer, site & 0xffffu);
       return false;
