@@ -388,6 +388,11 @@ def run_c3(args):
             line["allreduce_check"] = ar_check
         if e2e is not None:
             line["e2e"] = e2e
+            if world == 1 and not args.no_configs:
+                # the drop-in C++ path: the cfg2 region through C3KernelRegistry::executeFusedWithInputs
+                # with host tensors (copies and allocations per call, synchronous), beside the
+                # pipelined C-ABI figure above
+                line["e2e"]["api_region_cfg2"] = run_api_drive(["region", 8192, 4096, 4096, 10])
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         if world == 1 and not args.no_configs:
@@ -400,12 +405,30 @@ def run_c3(args):
         dist.destroy_process_group()
     bad = (ar_check is not None and not ar_check["ok"])
     if rank == 0 and "configs" in line:
-        bad = bad or not all(c["parity"]["ok"] for c in line["configs"].values())
+        bad = bad or not all(c["parity"]["ok"] for c in line["configs"].values() if "parity" in c)
     if bad:
         print("error: a correctness check in the benchmark failed (see allreduce_check / configs.*.parity)",
               file=sys.stderr)
         return 1
     return 0
+
+
+def run_api_drive(mode_args, timeout=600):
+    """Runs tests/cpp/api_drive (built on first use: the C++ mirror of the C3 API driven as a host
+    framework drives it) and returns its JSON record, or a record saying why it did not run."""
+    import subprocess
+    try:
+        from tests.cpp import build as cpp_build
+        exe = cpp_build.build_drive()
+        r = subprocess.run([str(exe)] + [str(a) for a in mode_args], capture_output=True, text=True,
+                           timeout=timeout)
+        lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        rec = json.loads(lines[-1]) if lines else {"error": (r.stderr or r.stdout)[-500:]}
+        rec["rc"] = r.returncode
+        rec["ok"] = r.returncode == 0  # its own parity checks and hit counts passed
+        return rec
+    except Exception as exc:  # reported in the line, never silently dropped
+        return {"error": repr(exc)[:500], "rc": None}
 
 
 def _host_threads() -> int:
@@ -729,6 +752,9 @@ def run_configs(dev, peak_burst, hbm, cpu_cores, cpu_fwd=None):
                                    "serial matmul path)"},
         "parity": {"logits_bit_exact": logits_exact, "loss_rel": loss_err, "params_max_rel": perr, "tol": 1e-5,
                    "ok": bool(logits_exact and loss_err <= 1e-5 and perr <= 1e-5)}}
+    # ---- cfg1 through the C3 API: the training loop a host framework runs, dispatched through
+    # the hot-path manager, the region and kernel registries and the backward capture
+    out["cfg1_mlp_step_api"] = run_api_drive(["mlp", 50])
     del flush_buf
     torch.cuda.empty_cache()
     return out

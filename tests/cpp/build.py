@@ -34,6 +34,32 @@ def build() -> Path:
     return OUT
 
 
+DRIVE = HERE / "_build" / "api_drive"
+
+
+def build_drive() -> Path:
+    """tests/cpp/api_drive.cpp: the C3 API driven as a host framework does (the cfg1 training loop
+    through the registries, the cfg2 region with host tensors), for the benchmark's API legs."""
+    sys.path.insert(0, str(ROOT))
+    from c3_b200 import build as lib_build
+    import oracle
+    lib = lib_build.build()
+    olib = oracle.build()
+    src = HERE / "api_drive.cpp"
+    headers = list((ROOT / "c3_b200" / "csrc" / "host").rglob("*.h")) + [ROOT / "include" / "c3cu.h"]
+    if DRIVE.exists() and all(DRIVE.stat().st_mtime >= p.stat().st_mtime for p in [src, lib, olib] + headers):
+        return DRIVE
+    DRIVE.parent.mkdir(exist_ok=True)
+    cmd = ["g++", "-std=c++17", "-O2", "-Wall", "-pthread", str(src), "-o", str(DRIVE),
+           f"-I{ROOT / 'c3_b200' / 'csrc' / 'host'}", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
+           f"-L{lib.parent}", "-lc3cu", f"-Wl,-rpath,{lib.parent}", f"-L{olib.parent}", "-loracle",
+           f"-Wl,-rpath,{olib.parent}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{' '.join(cmd)}\n{r.stderr}")
+    return DRIVE
+
+
 SANITIZERS = {"thread": "test_host_api_tsan", "address,undefined": "test_host_api_asan"}
 
 
