@@ -221,7 +221,7 @@ class LinearReluTrainStep:
 
     def __init__(self, m: int, n: int, k: int, device: torch.device, grad_dtype=torch.bfloat16,
                  collective: str = "auto", group=None, chunks: int = 1, num_ctas: int = 16,
-                 reserve_sms: int = 0):
+                 reserve_sms: int = 0, overlap_dx: bool = False):
         from . import _lib
         self.m, self.n, self.k = m, n, k
         self.device = torch.device(device)
@@ -236,6 +236,12 @@ class LinearReluTrainStep:
         self.dZ = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
         self.dX = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
         self.comm = torch.cuda.Stream(dev)
+        # overlap_dx: dX (which needs only dZ and W) runs on its own stream beside dW, so its tiles
+        # fill the SMs that dW's last wave leaves idle
+        self.overlap_dx = overlap_dx
+        self.side = torch.cuda.Stream(dev) if overlap_dx else None
+        self._ev_dz = torch.cuda.Event()
+        self._ev_dx = torch.cuda.Event()
         self._ev_band = [torch.cuda.Event() for _ in self.bands]
         self._ev_done = torch.cuda.Event()
         self._sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -263,8 +269,42 @@ class LinearReluTrainStep:
                 e.record(comp)
                 phases.setdefault(name, []).append(e)
 
+        def mark_on(name, stream):
+            if record:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(stream)
+                phases.setdefault(name, []).append(e)
+
+        def events():
+            out = {p: (phases[p][0], phases[p][1]) for p in self.PHASES}
+            if "dwdx" in phases:
+                out["dwdx"] = (phases["dwdx"][0], phases["dwdx"][1])
+            return StepEvents(out, ar)
+
         mark("fwd"); linear.forward(X, W, b, "nk", self.Y, self.mask); mark("fwd")
         mark("prepass"); linear.relu_mask_db(dY, self.mask, self.dZ, self.db); mark("prepass")
+        if self.overlap_dx:
+            # dW (with its sum over the ranks when fused) on the compute stream, dX beside it;
+            # "dwdx" spans both
+            self._ev_dz.record(comp)
+            self.side.wait_event(self._ev_dz)
+            mark("dwdx")
+            mark("dw")
+            if self.sync.fused:
+                self.sync.gemm_dw_reduce_(self.dZ, X, comp)
+            else:
+                linear.gemm(self.dZ, X, True, True, self.epi, self.dW, M=self.n, N=self.k, K=self.m)
+            mark("dw")
+            with torch.cuda.stream(self.side):
+                mark_on("dx", self.side)
+                linear.grad_input(self.dZ, W, "nk", self.dX)
+                mark_on("dx", self.side)
+            self._ev_dx.record(self.side)
+            comp.wait_event(self._ev_dx)
+            mark("dwdx")
+            if self.world > 1 and not self.sync.fused:
+                self.sync.reduce_((0, self.n), with_db=True, stream=comp)
+            return events() if record else None
         mark("dw")
         m, k = self.m, self.k
         if self.sync.fused:
@@ -272,9 +312,7 @@ class LinearReluTrainStep:
             self.sync.gemm_dw_reduce_(self.dZ, X, comp)
             mark("dw")
             mark("dx"); linear.grad_input(self.dZ, W, "nk", self.dX); mark("dx")
-            if record:
-                return StepEvents({p: (phases[p][0], phases[p][1]) for p in self.PHASES}, ar)
-            return None
+            return events() if record else None
         for i, (r0, r1) in enumerate(self.bands):
             linear.gemm(self.dZ[:, r0:r1], X, True, True, self.epi, self.dW[r0:r1], M=r1 - r0, N=k, K=m)
             if self.world > 1:
@@ -299,9 +337,7 @@ class LinearReluTrainStep:
             lib.c3cu_set_gemm_max_ctas(0)
         if self.world > 1:
             comp.wait_event(self._ev_done)
-        if record:
-            return StepEvents({p: (phases[p][0], phases[p][1]) for p in self.PHASES}, ar)
-        return None
+        return events() if record else None
 
 
 def default_overlap(world: int) -> tuple[int, int]:
