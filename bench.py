@@ -267,7 +267,7 @@ def run_c3(args):
     chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "1")))
     ar_ctas, ar_sms = default_overlap(world)
     reserve = int(os.environ.get("C3_BENCH_AR_SMS", str(ar_sms))) if world > 1 else 0
-    overlap_dx = os.environ.get("C3_DX_OVERLAP", "0") == "1"
+    overlap_dx = os.environ.get("C3_DX_OVERLAP", "1") == "1"  # dX beside dW (measured +1.7% at N=1)
     train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
                                 collective="auto" if world == 1 else ar_env,
                                 chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", str(ar_ctas))),
