@@ -26,6 +26,17 @@ bool deviceAvailable();
 void* allocDevice(size_t bytes);
 void freeDevice(void* p, cudaStream_t stream);
 
+// Copies between pageable host memory (a host framework's tensors) and device memory on
+// `stream`. Large copies go through the library's pinned staging buffers in chunks: a pool of
+// host threads copies one chunk between the host tensor and a staging buffer while the DMA of
+// the neighbouring chunk runs, so the link moves pinned-speed transfers although the host
+// tensor itself is not pinned. copyToDevice returns once `src` may be reused (the last DMA may
+// still be in flight on `stream`); copyToHost returns once `dst` holds the data. Small copies
+// (under 4 MiB) are plain cudaMemcpyAsync calls. Large copies from different host threads are
+// serialised on the staging buffers.
+void copyToDevice(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+void copyToHost(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
 // Throws std::runtime_error("<what>: <message>") when rc != 0 (a C3CU_ERR_* status).
 void checkAbi(int rc, const char* what);
 // Throws on a CUDA runtime error.

@@ -81,11 +81,15 @@ Tensor Tensor::to(DeviceType device) const {
     return out;
   }
   cudaStream_t s = ct::c3::cuda::currentStream();
-  const cudaMemcpyKind kind = device_ == DeviceType::kCPU    ? cudaMemcpyHostToDevice
-                              : device == DeviceType::kCPU ? cudaMemcpyDeviceToHost
-                                                           : cudaMemcpyDeviceToDevice;
-  ct::c3::cuda::checkCuda(cudaMemcpyAsync(out.data(), data(), bytes, kind, s), "Tensor::to");
-  if (device == DeviceType::kCPU || device_ == DeviceType::kCPU)
-    ct::c3::cuda::checkCuda(cudaStreamSynchronize(s), "Tensor::to: synchronize");
+  if (device_ == DeviceType::kCPU) {
+    // host -> device through the staging pipeline; `out` is stream-ordered on `s`
+    ct::c3::cuda::copyToDevice(out.data(), data(), bytes, s);
+    return out;
+  }
+  if (device == DeviceType::kCPU) {
+    ct::c3::cuda::copyToHost(out.data(), data(), bytes, s);
+    return out;
+  }
+  ct::c3::cuda::checkCuda(cudaMemcpyAsync(out.data(), data(), bytes, cudaMemcpyDeviceToDevice, s), "Tensor::to");
   return out;
 }

@@ -606,6 +606,19 @@ TEST(gpu_region_fp32_is_bit_exact_through_registry, true) {
   }
 }
 
+TEST(gpu_host_tensor_staging_round_trip, true) {
+  // Host <-> device copies of a host framework's (pageable) tensors: large ones go through the
+  // pinned staging pipeline in chunks (ragged last chunk here), small ones directly.
+  for (size_t n : {size_t(3), size_t(1) << 20, (size_t(25) << 20) + 12345}) {
+    Tensor h(ShapeTag{}, {n}, DType::kFloat, DeviceType::kCPU);
+    for (size_t i = 0; i < n; ++i) h.data_write<float>()[i] = static_cast<float>((i * 2654435761u) % 1000003u);
+    Tensor d = h.to(DeviceType::kCUDA);
+    Tensor d2 = d.to(DeviceType::kCUDA);  // device -> device
+    Tensor back = d2.to(DeviceType::kCPU);
+    CHECK(back.numel() == n && std::memcmp(back.data_read<float>(), h.data_read<float>(), n * 4) == 0);
+  }
+}
+
 TEST(gpu_backward_capture_relu_matmul_add, true) {
   std::mt19937 rng(9);
   const size_t M = 64, K = 96, N = 40;
