@@ -1,9 +1,15 @@
 #include "Tensor.h"
 
+#include <sys/mman.h>
+
 #include <cstdlib>
 #include <cstring>
 
 #include "C3/CudaRuntime.h"
+
+namespace {
+constexpr size_t kHugeBytes = size_t(2) << 20;
+}  // namespace
 
 struct Tensor::Storage {
   void* ptr = nullptr;
@@ -31,6 +37,14 @@ Tensor::Tensor(ShapeTag, const std::vector<size_t>& shape, DType dtype, DeviceTy
   if (device == DeviceType::kCUDA) {
     st->stream = ct::c3::cuda::currentStream();
     st->ptr = ct::c3::cuda::allocDevice(st->bytes);
+  } else if (st->bytes >= kHugeBytes) {
+    // Large host tensors sit on 2 MiB boundaries and ask for transparent huge pages: a result
+    // copied back from the GPU first-touches its pages, and 4 KiB pages would make that a
+    // page fault every 4 KiB.
+    const size_t rounded = (st->bytes + kHugeBytes - 1) / kHugeBytes * kHugeBytes;
+    st->ptr = std::aligned_alloc(kHugeBytes, rounded);
+    if (!st->ptr) throw std::bad_alloc();
+    madvise(st->ptr, rounded, MADV_HUGEPAGE);  // advisory: ignored where THP is off
   } else {
     const size_t rounded = ((st->bytes + 63) / 64) * 64;
     st->ptr = std::aligned_alloc(64, rounded > 0 ? rounded : 64);
