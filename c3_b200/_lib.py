@@ -56,6 +56,7 @@ _SIGNATURES = {
     "c3cu_convert": ([_vp, _i, _vp, _i, _i64, _vp], _i),
     "c3cu_set_gemm_max_ctas": ([_i], _i),
     "c3cu_set_gemm_variant": ([_i], _i),
+    "c3cu_set_split_wait_ns": ([ctypes.c_uint64], _i),
     "c3cu_gemm_tune_set": ([_i64, _i64, _i64, _i, _i, _i, _i], _i),
     "c3cu_gemm_tune_get": ([_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i)], _i),
     "c3cu_gemm_tune_clear": ([], _i),

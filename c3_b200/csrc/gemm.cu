@@ -76,6 +76,9 @@ constexpr size_t kSplitPartialFloats = static_cast<size_t>(kSplitMax) * 2 * gemm
 constexpr size_t kSplitWords = static_cast<size_t>(kSplitMax) * 2 * gemm2::kEpiWarps;
 constexpr size_t kSplitWsBytes = kSplitPartialFloats * 4 + 2 * kSplitWords * 4;
 
+// Limit on a split tile's wait for its partner's partial (c3cu_set_split_wait_ns).
+std::atomic<uint64_t> g_split_wait_ns{C3CU_WAIT_LIMIT_NS};
+
 // Bumped by gemm_invalidate_split_workspaces (after a recorded fault): a workspace cleared
 // under an older generation is cleared again before its next launch.
 std::atomic<uint32_t> g_split_generation{0};
@@ -148,6 +151,7 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
   const int k_blocks = (p.K + gemm2::BK - 1) / gemm2::BK;
   const gemm2::SplitPlan plan = gemm2::plan_split(tiles, clusters, k_blocks, variant, kSplitMax);
   Params q = p;
+  q.split_wait_ns = g_split_wait_ns.load(std::memory_order_relaxed);
   q.sk_mode = plan.sk_mode;
   q.sk_first = plan.sk_first;
   clusters = plan.clusters;
@@ -276,6 +280,7 @@ int gemm_general(const void* A, int64_t lda, int a_mn, const void* B, int64_t ld
   p.partial = nullptr;
   p.tickets = nullptr;
   p.ready = nullptr;
+  p.split_wait_ns = C3CU_WAIT_LIMIT_NS;
   p.ar_mc_out = nullptr;
   p.ar_mc_db = nullptr;
   p.ar_flags = nullptr;
@@ -300,6 +305,11 @@ int c3cu_set_gemm_max_ctas(int max_ctas) {
     return C3CU_ERR_INVALID;
   }
   c3cu::g_max_ctas = max_ctas;
+  return C3CU_OK;
+}
+
+int c3cu_set_split_wait_ns(uint64_t ns) {
+  c3cu::g_split_wait_ns.store(ns == 0 ? C3CU_WAIT_LIMIT_NS : ns, std::memory_order_relaxed);
   return C3CU_OK;
 }
 
@@ -403,6 +413,7 @@ int c3cu_gemm_dw_allreduce(const void* dZ, const void* X, void* dW, void* mc_dW,
   p.partial = nullptr;
   p.tickets = nullptr;
   p.ready = nullptr;
+  p.split_wait_ns = C3CU_WAIT_LIMIT_NS;
   p.ar_mc_out = mc_dW;
   p.ar_mc_db = mc_db;
   p.ar_flags = flags;

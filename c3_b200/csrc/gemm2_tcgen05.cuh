@@ -83,13 +83,13 @@ __device__ __forceinline__ void settle_inflight_copies() {
 // split >= 0 marks a tile that two clusters share as two K halves (the index of its fp32
 // partial slot); the two halves meet through a ticket in the epilogue.
 // Bounded acquire-wait for a split partner's "partial published" word.
-__device__ __forceinline__ bool wait_ready(const uint32_t* flag) {
+__device__ __forceinline__ bool wait_ready(const uint32_t* flag, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t v;
   while (true) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (v != 0u) return true;
-    if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_fault(kFaultWaitPeer, blockIdx.x & 0xffffu);
       return false;
     }
@@ -364,7 +364,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         adder = __shfl_sync(0xffffffffu, t, 0) != 0u;
         if (adder) {
           uint32_t ok = 1;
-          if (lane == 0) ok = wait_ready(&p.ready[word]) ? 1u : 0u;
+          if (lane == 0) ok = wait_ready(&p.ready[word], p.split_wait_ns) ? 1u : 0u;
           ok = __shfl_sync(0xffffffffu, ok, 0);
           uint32_t v;
           asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&p.ready[word]) : "memory");

@@ -70,6 +70,7 @@ struct Params {
   float* partial;
   uint32_t* tickets;
   uint32_t* ready;
+  uint64_t split_wait_ns;  // limit on the second half's wait for the first half's partial
   // kEpiBf16Allreduce: `out` is this rank's copy of a buffer bound to an NVLink multicast
   // object and `ar_mc_out` its multicast address; `ar_mc_db` the multicast address of an fp32
   // vector of `ar_db_count` elements summed alongside; `ar_flags` / `ar_mc_flags` this rank's

@@ -141,6 +141,13 @@ int c3cu_set_gemm_max_ctas(int max_ctas);
  * tickets) that the library keeps for that stream; capture such a launch in a CUDA graph only
  * after one uncaptured call on the same stream. */
 int c3cu_set_gemm_variant(int variant);
+/* Limit, in nanoseconds, on the wait of a split-K tile's second half for the first half's
+ * fp32 partial (process-wide, for launches that follow; 0 restores the default of 4 s). A
+ * test shortens it to make that wait run out, which records C3CU_ERR_FAULT (read with
+ * c3cu_fault_status) without faulting the GPU: the recovery path of a split GEMM whose partner
+ * was late. After c3cu_fault_status reports a fault, the next split launch on each stream
+ * clears its workspace first. No counterpart in the reference (its kernels never wait). */
+int c3cu_set_split_wait_ns(uint64_t ns);
 /* Per-shape variant table filled by a tuner (the B200 counterpart of the reference's tile
  * auto-tuner, include/C3/AutoTuner.h:42-63, src/C3/C3Engine.cpp:1577-1651): calls of exactly
  * (M, N, K, a_mn, b_mn, epilogue) use `variant` instead of the process-wide one. */

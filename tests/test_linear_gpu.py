@@ -383,3 +383,35 @@ def test_fused_dw_allreduce_single_rank_is_the_dw_gemm(cuda_device):
                                   ctypes.c_void_p(dW.data_ptr()), None, None, 0, None, None, 0,
                                   M, N, K, 0, 2, 0, s)
     assert rc == -1 and "null" in _lib.last_error()
+
+
+def test_split_k_recovers_after_a_partner_wait_runs_out(cuda_device):
+    """A split-K tile's second half that gives up waiting for the first half's partial (here:
+    the wait limit shortened to 1 ns through c3cu_set_split_wait_ns, no GPU fault) records
+    C3CU_ERR_FAULT. The late partner may leave its tile's ticket words set; after the fault is
+    read, the next launch clears the split workspace, so the same GEMM is bit-identical again."""
+    import ctypes
+
+    from c3_b200 import _lib
+    L = _lib.load()
+    M, N, K = 16384, 4096, 4096  # dW of cfg3: 256 tiles, the last wave split in K halves
+    dZ = randn((M, N), 1e-2, 51).to(cuda_device)
+    X = randn((M, K), 1.0, 52).to(cuda_device)
+    ref = linear.grad_weight(dZ, X, "nk")
+    torch.cuda.synchronize()
+    code = ctypes.c_uint32(0)
+    faulted = False
+    try:
+        assert L.c3cu_set_split_wait_ns(1) == 0
+        for _ in range(8):
+            linear.grad_weight(dZ, X, "nk")
+            if L.c3cu_fault_status(ctypes.byref(code)) == -4:  # C3CU_ERR_FAULT, read and cleared
+                faulted = True
+                break
+    finally:
+        assert L.c3cu_set_split_wait_ns(0) == 0
+    assert faulted, "no split tile's second half ever arrived before its partner published"
+    for _ in range(2):
+        out = linear.grad_weight(dZ, X, "nk")
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
