@@ -237,6 +237,8 @@ def run_c3(args):
     from c3_b200.data_parallel import LinearReluTrainStep, default_overlap, env_grad_dtype, shard_rows
     L = c3_b200.load()
     c3_b200.device_check()
+    launch_overlap = int(os.environ.get("C3_LAUNCH_OVERLAP", "0"))  # c3cu_set_launch_overlap (PDL)
+    c3_b200._lib.check(L.c3cu_set_launch_overlap(launch_overlap), "c3cu_set_launch_overlap")
     gemm_variant = int(os.environ.get("C3_GEMM_VARIANT", "0"))  # c3cu_set_gemm_variant
     if gemm_variant:
         c3_b200._lib.check(L.c3cu_set_gemm_variant(gemm_variant), "c3cu_set_gemm_variant")
@@ -362,6 +364,7 @@ def run_c3(args):
                        "grad_dtype": {"dW": "bf16" if grad_bf16 else "fp32", "db": "fp32"},
                        "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
                        "dx_beside_dw": overlap_dx,
+                       "programmatic_dependent_launch": bool(launch_overlap),
                        "allreduce": {"fused": "dW GEMM that sums dW and db over the ranks in its epilogue "
                                               "(c3cu_gemm_dw_allreduce: each finished tile reduced in the "
                                               "NVSwitch with multimem.ld_reduce/st while later tiles run)",

@@ -57,6 +57,7 @@ _SIGNATURES = {
     "c3cu_set_gemm_max_ctas": ([_i], _i),
     "c3cu_set_gemm_variant": ([_i], _i),
     "c3cu_set_split_wait_ns": ([ctypes.c_uint64], _i),
+    "c3cu_set_launch_overlap": ([_i], _i),
     "c3cu_gemm_tune_set": ([_i64, _i64, _i64, _i, _i, _i, _i], _i),
     "c3cu_gemm_tune_get": ([_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i)], _i),
     "c3cu_gemm_tune_clear": ([], _i),

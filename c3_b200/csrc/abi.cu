@@ -27,6 +27,10 @@ namespace {
 thread_local std::string g_last_error;
 }
 
+// Programmatic dependent launch of the GEMM and pre-pass kernels (c3cu_set_launch_overlap).
+std::atomic<bool> g_pdl{false};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+
 void set_error(const char* fmt, ...) {
   char buf[1024];
   va_list ap;
@@ -141,6 +145,15 @@ extern "C" {
 int c3cu_version(void) { return 1; }
 
 const char* c3cu_last_error(void) { return c3cu::g_last_error.c_str(); }
+
+int c3cu_set_launch_overlap(int enable) {
+  if (enable != 0 && enable != 1) {
+    c3cu::set_error("set_launch_overlap: expected 0 or 1, got %d", enable);
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::g_pdl.store(enable != 0, std::memory_order_relaxed);
+  return C3CU_OK;
+}
 
 int c3cu_device_check(void) { return c3cu::require_sm100(); }
 

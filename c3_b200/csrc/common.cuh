@@ -67,6 +67,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may
+// start (its prologue: barrier init, TMEM allocation, descriptor prefetch) while the previous
+// kernel on the stream drains; pdl_wait blocks until that kernel has completed and its memory
+// is visible, so no global memory is read or written before it. Without that launch attribute
+// both are no-ops. pdl_launch_dependents lets the next kernel on the stream be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -141,6 +141,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  pdl_wait();  // the previous kernel on the stream has completed (no-op without PDL)
+  pdl_launch_dependents();
 
   if (col < N) {
     const bool vec = vec_ok && (col + 8 <= N);
@@ -302,10 +304,10 @@ int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, in
   const int vec_ok = aligned16(in) && (!MASKED || aligned16(dz)) && ((N * esize) % 16 == 0);
   const int ldm = static_cast<int>((N + 31) / 32);
   dim3 grid(static_cast<unsigned>(strips), static_cast<unsigned>(rbs));
-  colsum_kernel<MASKED><<<grid, kWarps * 32, 0, st>>>(in, mask, static_cast<__nv_bfloat16*>(dz), out,
-                                                     static_cast<int>(M), static_cast<int>(N), ldm,
-                                                     static_cast<int>(rpb), partials, tickets, vec_ok);
-  return cuda_status(cudaGetLastError(), "column sum: launch");
+  return cuda_status(launch_kernel(colsum_kernel<MASKED>, grid, dim3(kWarps * 32), 0, st, in, mask,
+                                   static_cast<__nv_bfloat16*>(dz), out, static_cast<int>(M),
+                                   static_cast<int>(N), ldm, static_cast<int>(rpb), partials, tickets, vec_ok),
+                     "column sum: launch");
 }
 
 // ------------------------------------------------------------------ cfg4 chain

@@ -159,8 +159,9 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
     rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
     if (rc != C3CU_OK) return rc;
   }
-  kern<<<2 * clusters, gemm2::kThreads, gemm2::SMEM_BYTES, stream>>>(ta, tb, q);
-  return cuda_status(cudaGetLastError(), "gemm2: launch");
+  return cuda_status(launch_kernel(kern, dim3(2 * clusters), dim3(gemm2::kThreads), gemm2::SMEM_BYTES, stream,
+                                   ta, tb, q),
+                     "gemm2: launch");
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -191,8 +192,8 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   const int cap = g_max_ctas;
   if (cap > 0 && cap < sms) sms = cap;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, gemm::kThreads, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
-  return cuda_status(cudaGetLastError(), "gemm: launch");
+  return cuda_status(launch_kernel(kern, dim3(grid), dim3(gemm::kThreads), gemm::SMEM_BYTES, stream, ta, tb, p),
+                     "gemm: launch");
 }
 
 int dispatch(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,

@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/c3cu.h"
 
@@ -44,6 +45,27 @@ int encode_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint
 // adder has reset them), so every pooled split workspace is cleared again on its stream before
 // its next launch.
 void gemm_invalidate_split_workspaces();
+
+// Whether GEMM and pre-pass kernels are launched with programmatic dependent launch
+// (c3cu_set_launch_overlap; off by default).
+bool pdl_enabled();
+
+// Launches `kern` on `stream`, with programmatic stream serialization when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
 

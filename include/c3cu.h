@@ -148,6 +148,11 @@ int c3cu_set_gemm_variant(int variant);
  * was late. After c3cu_fault_status reports a fault, the next split launch on each stream
  * clears its workspace first. No counterpart in the reference (its kernels never wait). */
 int c3cu_set_split_wait_ns(uint64_t ns);
+/* Programmatic dependent launch for the GEMM and pre-pass kernels (process-wide; 0 = off, the
+ * default): each such kernel may be scheduled while the previous kernel on its stream drains,
+ * runs its prologue (barrier initialisation, TMEM allocation, descriptor prefetch) and then
+ * waits for that kernel's completion before it touches global memory. Results are unchanged. */
+int c3cu_set_launch_overlap(int enable);
 /* Per-shape variant table filled by a tuner (the B200 counterpart of the reference's tile
  * auto-tuner, include/C3/AutoTuner.h:42-63, src/C3/C3Engine.cpp:1577-1651): calls of exactly
  * (M, N, K, a_mn, b_mn, epilogue) use `variant` instead of the process-wide one. */

@@ -415,3 +415,35 @@ def test_split_k_recovers_after_a_partner_wait_runs_out(cuda_device):
         out = linear.grad_weight(dZ, X, "nk")
         torch.cuda.synchronize()
         assert torch.equal(out, ref)
+
+
+def test_launch_overlap_keeps_bits(cuda_device):
+    """With programmatic dependent launch (c3cu_set_launch_overlap) each GEMM / pre-pass kernel
+    may start its prologue while the previous one drains, but waits for it before touching
+    memory: the training step's outputs are bit-identical with it on and off."""
+    from c3_b200 import _lib
+    L = _lib.load()
+    M, N, K = 2048, 1024, 768
+    X = randn((M, K), 1.0, 61).to(cuda_device)
+    W = randn((N, K), 0.05, 62).to(cuda_device)
+    b = randn((N,), 0.05, 63, torch.float32).to(cuda_device)
+    dY = randn((M, N), 1e-2, 64).to(cuda_device)
+
+    def step():
+        Y, mask = linear.forward(X, W, b)
+        dZ, db = linear.relu_mask_db(dY, mask)
+        dW = linear.grad_weight(dZ, X, "nk")
+        dX = linear.grad_input(dZ, W, "nk")
+        return Y, mask, dZ, db, dW, dX
+
+    ref = step()
+    torch.cuda.synchronize()
+    try:
+        assert L.c3cu_set_launch_overlap(1) == 0
+        for _ in range(3):
+            got = step()
+        torch.cuda.synchronize()
+    finally:
+        assert L.c3cu_set_launch_overlap(0) == 0
+    for r, g in zip(ref, got):
+        assert torch.equal(r, g)
