@@ -53,6 +53,8 @@ _SIGNATURES = {
     "c3cu_matmul_f32": ([_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp, _i64, _i, _vp], _i),
     "c3cu_region_fwd_f32": ([_vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i, _vp], _i),
     "c3cu_sum_rows_f32_exact": ([_vp, _vp, _i64, _i64, _vp], _i),
+    "c3cu_matmul_relu_bwd_f32": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp], _i),
+    "c3cu_matmul_colsum_f32": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp], _i),
     "c3cu_convert": ([_vp, _i, _vp, _i, _i64, _vp], _i),
     "c3cu_set_gemm_max_ctas": ([_i], _i),
     "c3cu_set_gemm_variant": ([_i], _i),

@@ -7,6 +7,14 @@
 //                            and bit mask (src/C3/MLIRKernelGen.cpp:610-768)
 //   * c3cu_sum_rows_f32_exact — SumReduce axis 0 in the reference's row order
 //                            (src/C3/C3DialectLowering.cpp:382-465)
+//   * c3cu_matmul_relu_bwd_f32 — the MatMul backward dA (grad @ B^T) with the next ReLU
+//                            backward Mul(Gt(z, 0), .) applied to each result
+//                            (src/C3/C3BackwardCapture.cpp:501-528, 681-723)
+//   * c3cu_matmul_colsum_f32 — the MatMul backward dB (A^T @ grad) together with the Add
+//                            backward's SumReduce of grad (src/C3/C3BackwardCapture.cpp:618-644):
+//                            the column sums are one more output row whose A entries are 1, so
+//                            they accumulate in the same k order, (0 + 1*g0) + 1*g1 ..., which
+//                            is bit for bit SumReduce's (0 + g0) + g1 ...
 // Register tiling changes which thread computes an element, never the order of the k
 // reduction of that element, so these kernels reproduce the reference's results bit for
 // bit (expf/tanhf of the sigmoid/tanh activations aside, which use CUDA's libm).
@@ -28,6 +36,14 @@ __device__ __forceinline__ float load_a(const float* A, int i, int k, int M, int
   return TA ? A[(int64_t)k * M + i] : A[(int64_t)i * K + k];
 }
 
+// A with one extra row of ones (row M): the column sums of B come out as output row M.
+template <bool TA, bool TB>
+__device__ __forceinline__ float load_a_ones(const float* A, int i, int k, int M, int K) {
+  if (k >= K || i > M) return 0.f;
+  if (i == M) return 1.f;
+  return TA ? A[(int64_t)k * M + i] : A[(int64_t)i * K + k];
+}
+
 template <bool TA, bool TB>
 __device__ __forceinline__ float load_b(const float* B, int k, int j, int K, int N) {
   if (j >= N || k >= K) return 0.f;
@@ -36,6 +52,8 @@ __device__ __forceinline__ float load_b(const float* B, int k, int j, int K, int
 
 // MODE 0: out = act(bias_init + sum)     (plain c3.matmul)
 // MODE 1: s = sum + b[idx % bn]; out = maxnum(s, 0); z = s; mask bits (region forward)
+// MODE 2: out = (z[idx] > 0 ? 1 : 0) * sum (ReLU backward applied to dA; z is read, not written)
+// MODE 3: out = sum for rows < M; row M (A's entries 1) gives the column sums of B into z
 template <bool TA, bool TB, int MODE, int R>
 __global__ void __launch_bounds__(256)
     sgemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B,
@@ -68,7 +86,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int r = 0; r < LD; ++r) {
       const int e = threadIdx.x + r * 256;
-      ra[r] = load_a<TA, TB>(A, m0 + e / TK, k0 + e % TK, M, K);  // A tile: [TM][TK]
+      ra[r] = MODE == 3 ? load_a_ones<TA, TB>(A, m0 + e / TK, k0 + e % TK, M, K)
+                        : load_a<TA, TB>(A, m0 + e / TK, k0 + e % TK, M, K);  // A tile: [TM][TK]
       rb[r] = load_b<TA, TB>(B, k0 + e / TN, n0 + e % TN, K, N);  // B tile: [TK][TN]
     }
   };
@@ -105,14 +124,21 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < R; ++i) {
     const int row = m0 + ty * R + i;
-    if (row >= M) continue;
+    if (row > M || (row == M && MODE != 3)) continue;
 #pragma unroll
     for (int j = 0; j < R; ++j) {
       const int col = n0 + tx * R + j;
       if (col >= N) continue;
       const int64_t idx = (int64_t)row * N + col;
       const float t = acc[i][j];
-      if (MODE == 0) {
+      if (MODE == 3) {
+        if (row == M)
+          z[col] = t;
+        else
+          out[idx] = t;
+      } else if (MODE == 2) {
+        out[idx] = __fmul_rn(z[idx] > 0.f ? 1.f : 0.f, t);
+      } else if (MODE == 0) {
         float v = t;
         if (act == 1) {
           v = fmaxf(t, 0.f);
@@ -155,7 +181,8 @@ template <bool TA, bool TB, int MODE, int R>
 int launch_r(const float* A, const float* B, float* out, float* z, uint32_t* mask, const float* bias,
              int64_t bias_numel, int64_t M, int64_t K, int64_t N, int act, cudaStream_t st) {
   constexpr int T = 16 * R;
-  dim3 grid(static_cast<unsigned>((N + T - 1) / T), static_cast<unsigned>((M + T - 1) / T));
+  const int64_t rows = MODE == 3 ? M + 1 : M;  // MODE 3: the column-sum row
+  dim3 grid(static_cast<unsigned>((N + T - 1) / T), static_cast<unsigned>((rows + T - 1) / T));
   if (grid.y > 65535) {
     set_error("exact matmul: M=%lld too large", (long long)M);
     return C3CU_ERR_INVALID;
@@ -212,6 +239,36 @@ int c3cu_matmul_f32(const float* A, const float* B, float* out, int64_t M, int64
   }
   return c3cu::exact::dispatch<0>(transA != 0, transB != 0, A, B, out, nullptr, nullptr, bias,
                                   bias_numel, M, K, N, act, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_matmul_relu_bwd_f32(const float* A, const float* B, const float* z, float* out, int64_t M, int64_t K,
+                             int64_t N, int transA, int transB, c3cu_stream_t stream) {
+  int rc = c3cu::exact::check_sizes(M, K, N);
+  if (rc != C3CU_OK) return rc;
+  if (M == 0 || N == 0) return C3CU_OK;
+  if (!A || !B || !z || !out) {
+    c3cu::set_error("matmul_relu_bwd_f32: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  return c3cu::exact::dispatch<2>(transA != 0, transB != 0, A, B, out, const_cast<float*>(z), nullptr, nullptr,
+                                  0, M, K, N, 0, static_cast<cudaStream_t>(stream));
+}
+
+int c3cu_matmul_colsum_f32(const float* A, const float* B, float* out, float* colsum, int64_t M, int64_t K,
+                           int64_t N, int transA, int transB, c3cu_stream_t stream) {
+  int rc = c3cu::exact::check_sizes(M, K, N);
+  if (rc != C3CU_OK) return rc;
+  if (M >= INT32_MAX) {
+    c3cu::set_error("matmul_colsum_f32: M out of range");
+    return C3CU_ERR_INVALID;
+  }
+  if (N == 0) return C3CU_OK;
+  if (!out || !colsum || (K > 0 && (!B || (M > 0 && !A)))) {  // K = 0: nothing is read
+    c3cu::set_error("matmul_colsum_f32: null pointer");
+    return C3CU_ERR_INVALID;
+  }
+  return c3cu::exact::dispatch<3>(transA != 0, transB != 0, A, B, out, colsum, nullptr, nullptr, 0, M, K, N, 0,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 int c3cu_region_fwd_f32(const float* X, const float* B, const float* bias, int64_t bias_numel,

@@ -1,6 +1,8 @@
 """Bit-exact fp32 kernels (CUDA cores) restating the reference's fp32 loops: the c3.matmul
 sequential-k reduction (src/C3/C3DialectLowering.cpp:467-610), the MatMul+Add+ReLU region
-(src/C3/MLIRKernelGen.cpp:610-768) and SumReduce axis 0 (src/C3/C3DialectLowering.cpp:382-465)."""
+(src/C3/MLIRKernelGen.cpp:610-768), SumReduce axis 0 (src/C3/C3DialectLowering.cpp:382-465), and
+two pairs of the captured backward fused into one launch each (MatMul dA + the upstream ReLU
+backward; MatMul dB + the Add backward's SumReduce, src/C3/C3BackwardCapture.cpp:501-723)."""
 from __future__ import annotations
 
 import torch
@@ -65,3 +67,44 @@ def sum_rows(x: torch.Tensor) -> torch.Tensor:
     rc = _lib.load().c3cu_sum_rows_f32_exact(_p(x), _p(out), M, N, _stream(x.device))
     _lib.check(rc, "c3cu_sum_rows_f32_exact")
     return out
+
+
+def _mm_shapes(A, B, trans_a, trans_b):
+    M, K = (A.shape[1], A.shape[0]) if trans_a else (A.shape[0], A.shape[1])
+    N = B.shape[0] if trans_b else B.shape[1]
+    _f32(B, "B", 2, (N, K) if trans_b else (K, N))
+    return M, K, N
+
+
+def matmul_relu_bwd(A: torch.Tensor, B: torch.Tensor, z: torch.Tensor, trans_a: bool = False,
+                    trans_b: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = (z > 0 ? 1 : 0) * (A B): the MatMul backward dA followed by the upstream ReLU's
+    backward Mul(Gt(z, 0), .), in one launch, bit-exact."""
+    _f32(A, "A")
+    M, K, N = _mm_shapes(A, B, trans_a, trans_b)
+    _f32(z, "z", 2, (M, N))
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    _f32(out, "out", 2, (M, N))
+    rc = _lib.load().c3cu_matmul_relu_bwd_f32(_p(A), _p(B), _p(z), _p(out), M, K, N, int(trans_a), int(trans_b),
+                                              _stream(A.device))
+    _lib.check(rc, "c3cu_matmul_relu_bwd_f32")
+    return out
+
+
+def matmul_colsum(A: torch.Tensor, B: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
+                  out: torch.Tensor | None = None, colsum: torch.Tensor | None = None):
+    """(A B, column sums of b(k, j) over k): the MatMul backward dB and the Add backward's
+    SumReduce of the same gradient, in one launch, bit-exact."""
+    _f32(A, "A")
+    M, K, N = _mm_shapes(A, B, trans_a, trans_b)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    if colsum is None:
+        colsum = torch.empty(N, dtype=torch.float32, device=A.device)
+    _f32(out, "out", 2, (M, N))
+    _f32(colsum, "colsum", 1, (N,))
+    rc = _lib.load().c3cu_matmul_colsum_f32(_p(A), _p(B), _p(out), _p(colsum), M, K, N, int(trans_a),
+                                            int(trans_b), _stream(A.device))
+    _lib.check(rc, "c3cu_matmul_colsum_f32")
+    return out, colsum

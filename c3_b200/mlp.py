@@ -12,9 +12,9 @@ c3cu_ew_program, c3cu_sum_rows_f32_exact). The loss and the optimizer belong to 
 reference's host framework (not in its sources): c3cu_softmax_ce_f32 and c3cu_sgd_f32 use the
 textbook definitions.
 
-Weights use the reference's MatMul layout W [K, N] (fan_in rows). A step is 15 launches on
-the current stream; `capture()` records them once in a CUDA graph so that a step costs one
-graph launch.
+Weights use the reference's MatMul layout W [K, N] (fan_in rows). A step is 10 launches on
+the current stream (each MatMul backward fused with its neighbouring ReLU or Add backward);
+`capture()` records them once in a CUDA graph so that a step costs one graph launch.
 
 Data parallel (one process per GPU): each rank runs the step on its equal share of the global
 batch (`shard_batch`). The gradients and the loss share one flat fp32 buffer, so one all-reduce
@@ -31,15 +31,10 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from . import elementwise as ew
 from .data_parallel import shard_rows
 
 LAYERS = (784, 256, 128, 10)
 PARAM_NAMES = ("W1", "b1", "W2", "b2", "W3", "b3")
-
-# Mul(Gt(z, 0), grad): registers 0 = z, 1 = grad, 2 = constant 0 (table entry 0); the result
-# in register 3
-_RELU_BWD = [(ew.CONST, 2, 0, 0), (ew.GT, 3, 0, 2), (ew.MUL, 3, 3, 1)]
 
 
 def init_params(seed: int = 1234, device: torch.device | str = "cpu", layers=LAYERS) -> dict:
@@ -139,8 +134,8 @@ class MLPTrainStep:
         self.a1, self.z1 = f(batch, d1), f(batch, d1)
         self.a2, self.z2 = f(batch, d2), f(batch, d2)
         self.z3, self.dz3 = f(batch, d3), f(batch, d3)
-        self.da2, self.dz2 = f(batch, d2), f(batch, d2)
-        self.da1, self.dz1 = f(batch, d1), f(batch, d1)
+        self.dz2 = f(batch, d2)
+        self.dz1 = f(batch, d1)
         # gradients and loss in one buffer: one all-reduce covers them under data parallelism
         shapes = {k: tuple(params[k].shape) for k in PARAM_NAMES}
         self.flat = torch.zeros(flat_numel(shapes), dtype=torch.float32, device=dev)
@@ -168,10 +163,19 @@ class MLPTrainStep:
                                              ctypes.c_void_p(0), M, K, N, 0, self._stream())
         _lib.check(rc, "c3cu_region_fwd_f32")
 
-    def _colsum(self, x, out, M, N):
-        rc = _lib.load().c3cu_sum_rows_f32_exact(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                                                 M, N, self._stream())
-        _lib.check(rc, "c3cu_sum_rows_f32_exact")
+    def _mm_colsum(self, A, G, dW, db, M, K, N):
+        # dW [M, N] = A^T G (A stored [K, M]) and db = column sums of G [K, N]
+        rc = _lib.load().c3cu_matmul_colsum_f32(ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(G.data_ptr()),
+                                                ctypes.c_void_p(dW.data_ptr()), ctypes.c_void_p(db.data_ptr()),
+                                                M, K, N, 1, 0, self._stream())
+        _lib.check(rc, "c3cu_matmul_colsum_f32")
+
+    def _mm_relu_bwd(self, G, W, z, dz, M, K, N):
+        # dz [M, N] = (z > 0) * (G W^T), G [M, K], W [N, K]
+        rc = _lib.load().c3cu_matmul_relu_bwd_f32(ctypes.c_void_p(G.data_ptr()), ctypes.c_void_p(W.data_ptr()),
+                                                  ctypes.c_void_p(z.data_ptr()), ctypes.c_void_p(dz.data_ptr()),
+                                                  M, K, N, 0, 1, self._stream())
+        _lib.check(rc, "c3cu_matmul_relu_bwd_f32")
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -201,17 +205,14 @@ class MLPTrainStep:
                                              ctypes.c_void_p(self.loss.data_ptr()),
                                              ctypes.c_void_p(self.dz3.data_ptr()), B, d3, self._stream())
         _lib.check(rc, "c3cu_softmax_ce_f32")
-        # backward (captured-gradient order: output layer first)
-        self._mm(self.a2, self.dz3, g["W3"], d2, B, d3, 1, 0)
-        self._colsum(self.dz3, g["b3"], B, d3)
-        self._mm(self.dz3, p["W3"], self.da2, B, d3, d2, 0, 1)
-        ew.program([self.z2, self.da2], _RELU_BWD, [0.0], 3, B * d2, out=self.dz2)
-        self._mm(self.a1, self.dz2, g["W2"], d1, B, d2, 1, 0)
-        self._colsum(self.dz2, g["b2"], B, d2)
-        self._mm(self.dz2, p["W2"], self.da1, B, d2, d1, 0, 1)
-        ew.program([self.z1, self.da1], _RELU_BWD, [0.0], 3, B * d1, out=self.dz1)
-        self._mm(x, self.dz1, g["W1"], d0, B, d1, 1, 0)
-        self._colsum(self.dz1, g["b1"], B, d1)
+        # backward (captured-gradient order: output layer first), each MatMul backward fused
+        # with its neighbour: dW with the Add backward's SumReduce (db), dA with the upstream
+        # ReLU backward (dz = (z > 0) * dA); 5 launches instead of 10, the same bits
+        self._mm_colsum(self.a2, self.dz3, g["W3"], g["b3"], d2, B, d3)
+        self._mm_relu_bwd(self.dz3, p["W3"], self.z2, self.dz2, B, d3, d2)
+        self._mm_colsum(self.a1, self.dz2, g["W2"], g["b2"], d1, B, d2)
+        self._mm_relu_bwd(self.dz2, p["W2"], self.z1, self.dz1, B, d2, d1)
+        self._mm_colsum(x, self.dz1, g["W1"], g["b1"], d0, B, d1)
         # the one exchange step under data parallelism (NCCL for CUDA tensors)
         reduce_gradients(self.flat, self.world, self.group)
         # update

@@ -176,6 +176,18 @@ int c3cu_matmul_f32(const float* A, const float* B, float* out, int64_t M, int64
 int c3cu_region_fwd_f32(const float* X, const float* B, const float* bias, int64_t bias_numel,
                         float* out, float* z, uint32_t* mask, int64_t M, int64_t K, int64_t N,
                         int transB, c3cu_stream_t stream);
+/* The captured backward of two chained regions, fused pairwise, bit-exact:
+ * c3cu_matmul_relu_bwd_f32: out = (z > 0 ? 1 : 0) * (sum_k a(i,k) b(k,j)) -- MatMul backward dA
+ *   (grad @ B^T, src/C3/C3BackwardCapture.cpp:681-723) followed by the upstream ReLU's backward
+ *   Mul(Gt(z, 0), .) (:501-528); z [M][N] is that ReLU's input.
+ * c3cu_matmul_colsum_f32: out[M][N] = sum_k a(i,k) b(k,j) and colsum[j] = sum_k b(k,j) in k order
+ *   -- MatMul backward dB (A^T @ grad) with the Add backward's SumReduce of grad (:618-644,
+ *   src/C3/C3DialectLowering.cpp:382-465), both from one pass over grad.
+ * Operand indexing, transposes and the k order as in c3cu_matmul_f32. */
+int c3cu_matmul_relu_bwd_f32(const float* A, const float* B, const float* z, float* out, int64_t M, int64_t K,
+                             int64_t N, int transA, int transB, c3cu_stream_t stream);
+int c3cu_matmul_colsum_f32(const float* A, const float* B, float* out, float* colsum, int64_t M, int64_t K,
+                           int64_t N, int transA, int transB, c3cu_stream_t stream);
 /* Column sums in the reference's order (rows ascending), bit-exact; no workspace. */
 int c3cu_sum_rows_f32_exact(const float* in, float* out, int64_t M, int64_t N,
                             c3cu_stream_t stream);

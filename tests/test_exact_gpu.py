@@ -86,3 +86,26 @@ def test_exact_kernels_reproduce_golden_vectors(cuda_device):
             B = torch.from_numpy(arr(c["B"], (N, K) if tb else (K, N))).to(cuda_device)
             got = exact.matmul(A, B, bool(ta), bool(tb)).cpu().numpy().view(np.uint32).ravel()
             assert np.array_equal(got, np.array(c["out"], np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 10, 128), (128, 128, 256), (77, 33, 65)])
+def test_matmul_relu_bwd_bit_exact(cuda_device, M, K, N):
+    """MatMul backward dA (grad @ W^T, W stored [N, K]) fused with the upstream ReLU backward:
+    the same bits as the oracle's matmul followed by Mul(Gt(z, 0), .)."""
+    G, W, z = _rand((M, K), 30), _rand((N, K), 31), _rand((M, N), 32)
+    out = exact.matmul_relu_bwd(G.to(cuda_device), W.to(cuda_device), z.to(cuda_device), trans_b=True)
+    da = oracle.matmul(G.numpy(), W.numpy(), transB=True)
+    ref = oracle.relu_bwd(da, z.numpy())
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 128, 128), (784, 128, 256), (128, 128, 10), (5, 0, 7)])
+def test_matmul_colsum_bit_exact(cuda_device, M, K, N):
+    """MatMul backward dB (A^T @ grad, A stored [K, M]) and the Add backward's SumReduce of the
+    same grad from one launch: both bit-identical to the oracle's separate kernels."""
+    A, G = _rand((K, M), 40), _rand((K, N), 41)
+    dW, db = exact.matmul_colsum(A.to(cuda_device), G.to(cuda_device), trans_a=True)
+    ref_w = oracle.matmul(A.numpy(), G.numpy(), transA=True) if K > 0 else np.zeros((M, N), np.float32)
+    ref_b = oracle.sum_reduce(G.numpy(), 0) if K > 0 else np.zeros(N, np.float32)
+    assert np.array_equal(dW.cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
+    assert np.array_equal(db.cpu().numpy().view(np.uint32), ref_b.view(np.uint32))
