@@ -258,7 +258,9 @@ def run_c3(args):
     # (fp32 accumulation for bf16), unless C3_ALLREDUCE=nccl (process-group all_reduce).
     grad_dtype = env_grad_dtype()
     grad_bf16 = grad_dtype == torch.bfloat16
-    ar_env = os.environ.get("C3_ALLREDUCE", "fused")
+    # Default collective at N > 1: the separate in-switch all-reduce overlapped with dX (measured
+    # faster than the fused dW epilogue on 2 and 8 GPUs; C3_ALLREDUCE=fused selects that one).
+    ar_env = os.environ.get("C3_ALLREDUCE", "nvls")
     if ar_env not in ("fused", "nvls", "nccl", "group"):
         raise ValueError(f"C3_ALLREDUCE must be fused, nvls, nccl or group, got {ar_env!r}")
     if grad_dtype != torch.bfloat16 and ar_env == "fused":
@@ -269,7 +271,9 @@ def run_c3(args):
     chunks = max(1, int(os.environ.get("C3_BENCH_DW_CHUNKS", "1")))
     ar_ctas, ar_sms = default_overlap(world)
     reserve = int(os.environ.get("C3_BENCH_AR_SMS", str(ar_sms))) if world > 1 else 0
-    overlap_dx = os.environ.get("C3_DX_OVERLAP", "1") == "1"  # dX beside dW (measured +1.7% at N=1)
+    # dX beside dW: +1.7% at N=1. At N > 1 the default collective overlaps its all-reduce with
+    # dX instead (dX after dW, on SMs left free for the all-reduce).
+    overlap_dx = os.environ.get("C3_DX_OVERLAP", "1" if world == 1 else "0") == "1"
     train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
                                 collective="auto" if world == 1 else ar_env,
                                 chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", str(ar_ctas))),

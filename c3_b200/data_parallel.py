@@ -14,11 +14,12 @@ bands of dW (`dw_bands`): each band's all-reduce starts on a communication strea
 its GEMM ends, overlapped with the remaining bands and with the dX GEMM.
 
 `GradientSync` owns one rank's dW / db and sums them:
-- "fused" (default for a bf16 dW on GPUs): the dW GEMM itself sums dW and db over the ranks
-  (c3cu_gemm_dw_allreduce): each finished tile of dW is reduced in the NVSwitch while the
-  tensor cores work on the next ones, so the exchange needs no separate launch or stream;
-- "nvls": the library's in-switch all-reduce on NVLink-multicast memory (c3_b200.collective),
-  a separate kernel on a communication stream after the dW GEMM;
+- "nvls" (default on GPUs, "auto"): the library's in-switch all-reduce on NVLink-multicast memory
+  (c3_b200.collective), a separate kernel on a communication stream after the dW GEMM,
+  overlapped with dX;
+- "fused": the dW GEMM itself sums dW and db over the ranks (c3cu_gemm_dw_allreduce): each
+  finished tile of dW is reduced in the NVSwitch while the tensor cores work on the next ones, so
+  the exchange needs no separate launch or stream (measured slower than "nvls" on 2 and 8 GPUs);
 - "nccl": NCCL through the library's C ABI (c3cu_allreduce_grads on a communicator made by
   c3cu_nccl_comm_init), as a C++ host calls it;
 - "group": torch.distributed all_reduce on the process group (NCCL for CUDA tensors, gloo for
@@ -110,7 +111,7 @@ class GradientSync:
             try:
                 from .collective import NvlsAllReduce
                 if grad_dtype == torch.bfloat16:
-                    fused = collective in ("fused", "auto") and n > 128 and k % 8 == 0 and n % 4 == 0
+                    fused = collective == "fused" and n > 128 and k % 8 == 0 and n % 4 == 0
                     words = 4 + 16 * ((n + 255) // 256) * ((k + 255) // 256) if fused else 0
                     self.nvls = NvlsAllReduce(n, self.device, group=group, num_ctas=num_ctas,
                                               numel_bf16=n * k, ar_flag_words=words)
