@@ -58,21 +58,23 @@ def _traffic():
 
 
 class ClockSampler:
-    """Samples the SM clock, the clock-event (throttle) reasons and the instantaneous power
-    through NVML every `interval` seconds (0.5 ms by default) during the timed region. A sample
-    counts as under load unless NVML flags the GPU idle (clock-event reason gpu_idle); the
-    reported clock is the median of the samples under load."""
+    """Samples the SM clock and the clock-event (throttle) reasons through NVML every `interval`
+    seconds (0.5 ms by default) during the timed region, and the instantaneous power on a thread
+    of its own (that query can take milliseconds on some drivers). A clock sample counts as under
+    load unless NVML flags the GPU idle (clock-event reason gpu_idle); the reported clock is the
+    median of the samples under load."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
     def __init__(self, index: int, interval: float = 0.0005):
-        self.samples = []  # (sm_mhz, reason bits, power_w or None)
+        self.samples = []  # (sm_mhz, reason bits)
+        self.power = []
         self.max_mhz = None
         self.interval = interval
         self._stop = threading.Event()
-        self._t = None
+        self._threads = []
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -82,37 +84,40 @@ class ClockSampler:
         except Exception:  # no NVML: the line carries no clock record
             self._nv = None
 
-    def _power_w(self):
-        nv = self._nv
-        try:
-            v = nv.nvmlDeviceGetFieldValues(self._h, [nv.NVML_FI_DEV_POWER_INSTANT])[0]
-            if v.nvmlReturn == 0:
-                return v.value.uiVal / 1000.0
-        except Exception:
-            pass
-        return None
-
-    def _run(self):
+    def _run_clocks(self):
         nv = self._nv
         while not self._stop.is_set():
             try:
                 mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
                 bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((mhz, bits, self._power_w()))
+                self.samples.append((mhz, bits))
             except Exception:
                 pass
             self._stop.wait(self.interval)
 
+    def _run_power(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                v = nv.nvmlDeviceGetFieldValues(self._h, [nv.NVML_FI_DEV_POWER_INSTANT])[0]
+                if v.nvmlReturn == 0:
+                    self.power.append(v.value.uiVal / 1000.0)
+            except Exception:
+                pass
+            self._stop.wait(0.005)
+
     def __enter__(self):
         if self._nv is not None:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
+            for fn in (self._run_clocks, self._run_power):
+                t = threading.Thread(target=fn, daemon=True)
+                t.start()
+                self._threads.append(t)
         return self
 
     def __exit__(self, *exc):
         self._stop.set()
-        if self._t is not None:
-            self._t.join()
+        for t in self._threads:
+            t.join()
 
     def record(self):
         if self._nv is None or not self.samples:
@@ -120,15 +125,15 @@ class ClockSampler:
         busy = [s for s in self.samples if not s[1] & 0x1]
         use = busy or self.samples
         reasons = set()
-        for _, bits, _ in use:
+        for _, bits in use:
             reasons |= {name for b, name in self.REASONS.items() if bits & b}
-        power = [p for _, _, p in use if p is not None]
-        return {"sm_mhz": statistics.median(m for m, _, _ in use), "sm_max_mhz": self.max_mhz,
+        return {"sm_mhz": statistics.median(m for m, _ in use), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(reasons - {"gpu_idle"}), "samples": len(self.samples),
                 "samples_under_load": len(busy), "interval_ms": self.interval * 1e3,
-                "sm_mhz_min_under_load": min(m for m, _, _ in use),
-                "power_w_median": statistics.median(power) if power else None,
-                "power_w_max": max(power) if power else None,
+                "sm_mhz_min_under_load": min(m for m, _ in use),
+                "power_w_median": statistics.median(self.power) if self.power else None,
+                "power_w_max": max(self.power) if self.power else None,
+                "power_samples": len(self.power),
                 "load": "samples without NVML's gpu_idle clock-event reason"}
 
 
