@@ -59,22 +59,24 @@ def _traffic():
 
 class ClockSampler:
     """Samples the SM clock and the clock-event (throttle) reasons through NVML every `interval`
-    seconds (0.5 ms by default) during the timed region, and the instantaneous power on a thread
-    of its own (that query can take milliseconds on some drivers). A clock sample counts as under
-    load unless NVML flags the GPU idle (clock-event reason gpu_idle); the reported clock is the
-    median of the samples under load."""
+    seconds (0.5 ms by default) during the timed region. A sample counts as under load unless NVML
+    flags the GPU idle (clock-event reason gpu_idle); the reported clock is the median of the
+    samples under load. Power is not queried here: on this driver that query blocks for tens of
+    milliseconds, and at N > 1 a stalled rank stalls every rank's step. Only rank 0 samples."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, index: int, interval: float = 0.0005):
+    def __init__(self, index: int, interval: float = 0.0005, enabled: bool = True):
         self.samples = []  # (sm_mhz, reason bits)
-        self.power = []
         self.max_mhz = None
         self.interval = interval
         self._stop = threading.Event()
-        self._threads = []
+        self._t = None
+        self._nv = None
+        if not enabled:
+            return
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -84,7 +86,7 @@ class ClockSampler:
         except Exception:  # no NVML: the line carries no clock record
             self._nv = None
 
-    def _run_clocks(self):
+    def _run(self):
         nv = self._nv
         while not self._stop.is_set():
             try:
@@ -95,29 +97,16 @@ class ClockSampler:
                 pass
             self._stop.wait(self.interval)
 
-    def _run_power(self):
-        nv = self._nv
-        while not self._stop.is_set():
-            try:
-                v = nv.nvmlDeviceGetFieldValues(self._h, [nv.NVML_FI_DEV_POWER_INSTANT])[0]
-                if v.nvmlReturn == 0:
-                    self.power.append(v.value.uiVal / 1000.0)
-            except Exception:
-                pass
-            self._stop.wait(0.005)
-
     def __enter__(self):
         if self._nv is not None:
-            for fn in (self._run_clocks, self._run_power):
-                t = threading.Thread(target=fn, daemon=True)
-                t.start()
-                self._threads.append(t)
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
         return self
 
     def __exit__(self, *exc):
         self._stop.set()
-        for t in self._threads:
-            t.join()
+        if self._t is not None:
+            self._t.join()
 
     def record(self):
         if self._nv is None or not self.samples:
@@ -131,10 +120,7 @@ class ClockSampler:
                 "reasons": sorted(reasons - {"gpu_idle"}), "samples": len(self.samples),
                 "samples_under_load": len(busy), "interval_ms": self.interval * 1e3,
                 "sm_mhz_min_under_load": min(m for m, _ in use),
-                "power_w_median": statistics.median(self.power) if self.power else None,
-                "power_w_max": max(self.power) if self.power else None,
-                "power_samples": len(self.power),
-                "load": "samples without NVML's gpu_idle clock-event reason"}
+                "load": "samples without NVML's gpu_idle clock-event reason", "sampled_on": "rank 0's GPU"}
 
 
 def _dist_env():
@@ -309,7 +295,7 @@ def run_c3(args):
         dist.barrier()
     torch.cuda.synchronize()
     sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                           else local)
+                           else local, enabled=rank == 0)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with sampler:
