@@ -448,19 +448,17 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
-  if (attn::g_attn_variant == 0 || attn::g_attn_variant == 3 || attn::g_attn_variant == 4) {
+  if (attn::g_attn_variant == 0 || attn::g_attn_variant == 3) {
     // 64-key blocks: K / V tensor maps with 64-row boxes
     CUtensorMap tk64, tv64;
     if ((rc = attn::encode_bhsd(&tk64, K, B * H, S, 64)) != C3CU_OK) return rc;
     if ((rc = attn::encode_bhsd(&tv64, V, B * H, S, 64)) != C3CU_OK) return rc;
-    const bool ilp = attn::g_attn_variant == 4;
-    auto kern = ilp ? attn::flash_fwd3_kernel<true> : attn::flash_fwd3_kernel<false>;
-    static std::atomic<uint64_t> smem_set3{0}, smem_set4{0};
-    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), attn::SMEM_BYTES3, ilp ? smem_set4 : smem_set3,
-                              "flash_attn_fwd: set shared memory");
+    static std::atomic<uint64_t> smem_set3{0};
+    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd3_kernel), attn::SMEM_BYTES3,
+                              smem_set3, "flash_attn_fwd: set shared memory");
     if (rc != C3CU_OK) return rc;
-    kern<<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3, static_cast<cudaStream_t>(stream)>>>(
-        tq, tk64, tv64, p);
+    attn::flash_fwd3_kernel<<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
+                              static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
     return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
   }
   static std::atomic<uint64_t> smem_set2{0};
@@ -473,7 +471,7 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
 }
 
 extern "C" int c3cu_set_attn_variant(int variant) {
-  if (variant < 0 || variant > 4) {
+  if (variant < 0 || variant > 3) {
     c3cu::set_error("set_attn_variant: unknown variant %d", variant);
     return C3CU_ERR_INVALID;
   }

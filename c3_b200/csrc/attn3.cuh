@@ -24,12 +24,6 @@ constexpr int kThreads3 = 320;
 // smem: Q0 | Q1 | (K V) x stages | barriers
 constexpr uint32_t SMEM_BYTES3 = 2 * TILE_BYTES + KV_STAGES3 * 2 * KV_TILE3 + 32 * 8 + 1024;
 
-// kIlp (variant 4): the softmax thread's dependent chains are shortened. The next block's
-// scores are read from TMEM while this block's exponentials run (when its QK^T has already
-// completed), so the TMEM load latency leaves the critical path; the row maximum is an 8-way
-// tree and the row sum a 4-way one instead of 2-way chains. The arithmetic of each exponential
-// and the order in which P is written are unchanged; the row sum's association changes.
-template <bool kIlp>
 __global__ void __launch_bounds__(kThreads3, 1)
     flash_fwd3_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const Params p) {
@@ -197,38 +191,19 @@ __global__ void __launch_bounds__(kThreads3, 1)
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    uint32_t nxt[BKV3];     // kIlp: the next block's scores, loaded ahead
-    bool have_nxt = false;  // kIlp: nxt holds block j's scores
     for (int j = 0; j < n; ++j) {
       const uint32_t s_base = t_base + 64u * (j & 1);
+      if (!mbar_wait(&s_full[2 * t + (j & 1)], (j >> 1) & 1u, kFaultWaitAccFull)) { ok = false; break; }
+      tc_fence_after();
       float s[BKV3];
-      if (kIlp && have_nxt) {
-        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < BKV3; ++i) s[i] = __uint_as_float(nxt[i]);
-      } else {
-        if (!mbar_wait(&s_full[2 * t + (j & 1)], (j >> 1) & 1u, kFaultWaitAccFull)) { ok = false; break; }
-        tc_fence_after();
+      for (int c = 0; c < BKV3 / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(s_base + c * 32, r);
 #pragma unroll
-        for (int c = 0; c < BKV3 / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(s_base + c * 32, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-        }
-        tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
       }
-      have_nxt = false;
-      if (kIlp && j + 1 < n) {
-        // S_{t,j+1} sits in the other buffer; if its MMA has completed, start reading it now
-        if (mbar_try_wait(&s_full[2 * t + ((j + 1) & 1)], ((j + 1) >> 1) & 1u)) {
-          tc_fence_after();
-          const uint32_t n_base = t_base + 64u * ((j + 1) & 1);
-          tmem_ld_32x32b_x32(n_base, *reinterpret_cast<uint32_t(*)[32]>(&nxt[0]));
-          tmem_ld_32x32b_x32(n_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&nxt[32]));
-          have_nxt = true;
-        }
-      }
+      tmem_wait_ld();
       const int k0 = j * BKV3;
       if ((p.causal && k0 + BKV3 - 1 > row) || (k0 + BKV3 > p.S)) {
         const int lim = p.causal ? min(row, p.S - 1) : p.S - 1;
@@ -236,35 +211,20 @@ __global__ void __launch_bounds__(kThreads3, 1)
         for (int i = 0; i < BKV3; ++i)
           if (k0 + i > lim) s[i] = -INFINITY;
       }
-      float row_max;
-      if constexpr (kIlp) {
-        float mx[8];
+      float mx0 = s[0], mx1 = s[1];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) mx[u] = s[u];
-#pragma unroll
-        for (int i = 8; i < BKV3; i += 8)
-#pragma unroll
-          for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], s[i + u]);
-        row_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      } else {
-        float mx0 = s[0], mx1 = s[1];
-#pragma unroll
-        for (int i = 2; i < BKV3; i += 2) {
-          mx0 = fmaxf(mx0, s[i]);
-          mx1 = fmaxf(mx1, s[i + 1]);
-        }
-        row_max = fmaxf(mx0, mx1);
+      for (int i = 2; i < BKV3; i += 2) {
+        mx0 = fmaxf(mx0, s[i]);
+        mx1 = fmaxf(mx1, s[i + 1]);
       }
-      const float m_new = fmaxf(m_used, row_max * p.scale_log2);
+      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * p.scale_log2);
       const bool need = (m_used == -INFINITY) ? (m_new != -INFINITY) : (m_new > m_used + kRescaleThreshold);
       const float m_next = need ? m_new : m_used;
       const float alpha = need ? ((m_used == -INFINITY) ? 0.f : ex2(m_used - m_new)) : 1.f;
       const float base = (m_next == -INFINITY) ? 0.f : m_next;
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
       const float2 nb2 = make_float2(-base, -base);
-      float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                       make_float2(0.f, 0.f)};
+      float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < BKV3 / 32; ++c) {
         uint32_t w[16];
@@ -273,18 +233,12 @@ __global__ void __launch_bounds__(kThreads3, 1)
           float2 x = make_float2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
           x = ffma2(x, sc2, nb2);
           const float2 e = make_float2(ex2(x.x), ex2(x.y));
-          if constexpr (kIlp)
-            rs2[i & 3] = fadd2(rs2[i & 3], e);
-          else
-            rs2[0] = fadd2(rs2[0], e);
+          rs2 = fadd2(rs2, e);
           w[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st_32x32b_x16(s_base + c * 16, w);
       }
-      if constexpr (kIlp) {
-        rs2[0] = fadd2(fadd2(rs2[0], rs2[1]), fadd2(rs2[2], rs2[3]));
-      }
-      l = l * alpha + (rs2[0].x + rs2[0].y);
+      l = l * alpha + (rs2.x + rs2.y);
       // Rescaling O needs PV_{t,j-1} complete; unlike the single-buffer kernel, S_{t,j} was
       // issued before PV_{t,j-1}, so this wait can block.
       if (j > 0 && __any_sync(0xffffffffu, need)) {

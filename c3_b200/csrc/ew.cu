@@ -28,33 +28,6 @@ constexpr int kRowsPerBlock = 512;  // rows one block reduces before the cross-b
 #define C3CU_COLSUM_PREFETCH 1
 #endif
 constexpr bool kColsumPrefetch = C3CU_COLSUM_PREFETCH != 0;
-// Pre-pass staging (C3CU_PREPASS_BULK=1): each warp streams its dY row segments into a ring of
-// kRing shared-memory buffers with bulk copies (cp.async.bulk, this GPU's memory, no multicast),
-// so kRing rows per warp are in flight without holding registers. Off by default.
-#ifndef C3CU_PREPASS_BULK
-#define C3CU_PREPASS_BULK 0
-#endif
-constexpr bool kPrepassBulk = C3CU_PREPASS_BULK != 0;
-constexpr int kRing = 8;
-
-// Bounded wait used only while draining after a fault (ignores the fault word).
-__device__ __forceinline__ void ring_drain_wait(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS / 4) {
-      record_fault(kFaultDrain, blockIdx.x & 0xffffu);
-      return;
-    }
-  }
-}
-
-__device__ __forceinline__ void bulk_load_row(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // L2 prefetch of `bytes` (a multiple of 16) from a 16-byte-aligned global address; no data is
 // returned and no register is held.
@@ -171,54 +144,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   pdl_wait();  // the previous kernel on the stream has completed (no-op without PDL)
   pdl_launch_dependents();
 
-  bool staged = false;
-  if constexpr (MASKED && kPrepassBulk) {
-    // full 256-column strips with 16-byte-aligned rows: bulk-copy ring (whole warp, same path)
-    __shared__ __align__(128) uint8_t ring[kWarps][kRing][kColsPerWarp * 2];
-    __shared__ __align__(8) uint64_t ring_bar[kWarps][kRing];
-    if (vec_ok && strip * kColsPerWarp + kColsPerWarp <= N) {
-      staged = true;
-      uint64_t* bars = ring_bar[warp];
-      const int first = row0 + warp;
-      const int nrows = first < row1 ? (row1 - first + kWarps - 1) / kWarps : 0;
-      const char* seg0 = static_cast<const char*>(in) + static_cast<int64_t>(strip) * kColsPerWarp * 2;
-      const int64_t row_bytes = static_cast<int64_t>(N) * 2;
-      constexpr uint32_t kSeg = kColsPerWarp * 2;
-      if (lane == 0) {
-        for (int d = 0; d < kRing; ++d) mbar_init(&bars[d], 1);
-        fence_mbarrier_init();
-      }
-      __syncwarp();
-      auto issue = [&](int k) {
-        const int slot = k % kRing;
-        mbar_arrive_expect_tx(&bars[slot], kSeg);
-        bulk_load_row(ring[warp][slot], seg0 + static_cast<int64_t>(first + k * kWarps) * row_bytes, kSeg,
-                      &bars[slot]);
-      };
-      if (lane == 0)
-        for (int k = 0; k < min(kRing, nrows); ++k) issue(k);
-      int k = 0;
-      bool ok = true;
-      for (; k < nrows; ++k) {
-        const int slot = k % kRing;
-        if (!mbar_wait(&bars[slot], static_cast<uint32_t>(k / kRing) & 1u, kFaultWaitFull)) { ok = false; break; }
-        const int r = first + k * kWarps;
-        const uint4 q = reinterpret_cast<const uint4*>(ring[warp][slot])[lane];
-        uint32_t raw[8] = {q.x, q.y, q.z, q.w, 0u, 0u, 0u, 0u};
-        const uint32_t bits = __ldg(mask + (int64_t)r * ldm + (col >> 5)) >> (col & 31);
-        colsum_consume<MASKED>(dz, r, col, N, true, raw, bits, acc);
-        __syncwarp();  // every lane has read the slot before it is refilled
-        if (lane == 0 && k + kRing < nrows) issue(k + kRing);
-      }
-      if (!ok && lane == 0) {
-        // copies still in flight write this CTA's shared memory: let them land before exiting
-        for (int j = k; j < min(k + kRing, nrows); ++j)
-          ring_drain_wait(&bars[j % kRing], static_cast<uint32_t>(j / kRing) & 1u);
-      }
-      __syncwarp();
-    }
-  }
-  if (!staged && col < N) {
+  if (col < N) {
     const bool vec = vec_ok && (col + 8 <= N);
     int r = row0 + warp;
     // Rows of the next batch are prefetched into L2 (one bulk prefetch of the warp's row segment,

@@ -263,9 +263,7 @@ int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, fl
                         c3cu_stream_t stream);
 /* Attention kernel for the calls that follow (process-wide): 0 = default (3); 1 = one
  * 128-row query tile per CTA; 2 = two query tiles per CTA sharing each 128-key K / V block;
- * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM; 4 = variant 3
- * with shorter dependent chains in the softmax (next block's scores read from TMEM ahead,
- * tree-shaped row maximum and sum). */
+ * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM. */
 int c3cu_set_attn_variant(int variant);
 
 /* ------------------------------------------------------------------ fused dW GEMM + all-reduce
