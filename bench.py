@@ -57,59 +57,86 @@ def _traffic():
     return None
 
 
+_SAMPLER_SRC = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+interval = float(sys.argv[2])
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+out = []
+deadline = time.monotonic() + float(sys.argv[3])
+while time.monotonic() < deadline:
+    t = time.monotonic()
+    try:
+        out.append("%.6f %d %d" % (t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                   pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+    except Exception:
+        pass
+    if len(out) >= 64:
+        print("\n".join(out), flush=True)
+        out = []
+    time.sleep(interval)
+print("\n".join(out), flush=True)
+"""
+
+
 class ClockSampler:
     """Samples the SM clock and the clock-event (throttle) reasons through NVML every `interval`
-    seconds (0.5 ms by default) during the timed region. A sample counts as under load unless NVML
-    flags the GPU idle (clock-event reason gpu_idle); the reported clock is the median of the
-    samples under load. Power is not queried here: on this driver that query blocks for tens of
-    milliseconds, and at N > 1 a stalled rank stalls every rank's step. Only rank 0 samples."""
+    seconds (0.5 ms by default) from a separate process, and keeps the samples whose timestamps
+    fall inside the timed region. NVML queries made from the benchmark's own process held up its
+    kernel launches (at 8 GPUs a rank that launches late delays every rank's step); power is not
+    queried at all (on this driver that query blocks for tens of milliseconds). A sample counts as
+    under load unless NVML flags the GPU idle (clock-event reason gpu_idle); the reported clock is
+    the median of the samples under load. Only rank 0 samples."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, index: int, interval: float = 0.0005, enabled: bool = True):
+    def __init__(self, index: int, interval: float = 0.0005, enabled: bool = True, max_seconds: float = 120.0):
         self.samples = []  # (sm_mhz, reason bits)
         self.max_mhz = None
         self.interval = interval
-        self._stop = threading.Event()
-        self._t = None
-        self._nv = None
+        self.proc = None
+        self.t0 = self.t1 = None
         if not enabled:
             return
+        import subprocess
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, str(index), str(interval),
+                                          str(max_seconds)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            first = self.proc.stdout.readline().split()  # "max <MHz>": NVML is up and sampling
+            self.max_mhz = int(first[1]) if len(first) == 2 else None
+            if self.max_mhz is None:
+                self.proc.kill()
+                self.proc = None
         except Exception:  # no NVML: the line carries no clock record
-            self._nv = None
-
-    def _run(self):
-        nv = self._nv
-        while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((mhz, bits))
-            except Exception:
-                pass
-            self._stop.wait(self.interval)
+            self.proc = None
 
     def __enter__(self):
-        if self._nv is not None:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._t is not None:
-            self._t.join()
+        self.t1 = time.monotonic()
+        if self.proc is None:
+            return
+        self.proc.kill()
+        try:
+            rest, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            rest = ""
+        for ln in rest.splitlines():
+            parts = ln.split()
+            if len(parts) == 3:
+                t, mhz, bits = float(parts[0]), int(parts[1]), int(parts[2])
+                if self.t0 <= t <= self.t1:
+                    self.samples.append((mhz, bits))
 
     def record(self):
-        if self._nv is None or not self.samples:
+        if not self.samples:
             return None
         busy = [s for s in self.samples if not s[1] & 0x1]
         use = busy or self.samples
@@ -120,7 +147,8 @@ class ClockSampler:
                 "reasons": sorted(reasons - {"gpu_idle"}), "samples": len(self.samples),
                 "samples_under_load": len(busy), "interval_ms": self.interval * 1e3,
                 "sm_mhz_min_under_load": min(m for m, _ in use),
-                "load": "samples without NVML's gpu_idle clock-event reason", "sampled_on": "rank 0's GPU"}
+                "load": "samples without NVML's gpu_idle clock-event reason",
+                "sampled_on": "rank 0's GPU, from a separate process"}
 
 
 def _dist_env():
@@ -291,11 +319,12 @@ def run_c3(args):
     torch.cuda.synchronize()
     c3_b200.fault_status()
 
+    # the sampler process starts (and is sampling) before the ranks line up for the timed region
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local, enabled=rank == 0)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                           else local, enabled=rank == 0)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with sampler:

@@ -141,7 +141,7 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
                             "gemm2: set max dynamic shared memory");
   if (rc != C3CU_OK) return rc;
   const int tiles = ((p.M + gemm2::TM - 1) / gemm2::TM) * ((p.N + gemm2::TN - 1) / gemm2::TN);
-  int clusters = max_pair_clusters(kern, gemm2::SMEM_BYTES, gemm2::threads_for<EPI>());
+  int clusters = max_pair_clusters(kern, gemm2::SMEM_BYTES, gemm2::kThreads);
   if (clusters <= 0) clusters = sm_count() / 2;
   const int cap = g_max_ctas;
   if (cap > 0 && cap / 2 < clusters) clusters = cap / 2 > 0 ? cap / 2 : 1;
@@ -159,7 +159,7 @@ int launch_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const Pa
     rc = split_workspace(stream, &q.partial, &q.tickets, &q.ready);
     if (rc != C3CU_OK) return rc;
   }
-  return cuda_status(launch_kernel(kern, dim3(2 * clusters), dim3(gemm2::threads_for<EPI>()), gemm2::SMEM_BYTES, stream,
+  return cuda_status(launch_kernel(kern, dim3(2 * clusters), dim3(gemm2::kThreads), gemm2::SMEM_BYTES, stream,
                                    ta, tb, q),
                      "gemm2: launch");
 }

@@ -22,7 +22,6 @@
 //               quarter (warp w reads lanes 32 * (w % 4) ...), each on half of the 256
 //               columns; they release an accumulator by arriving on the leader's
 //               `acc_empty` barrier (16 arrivals: both CTAs).
-//   warps 10,11 (kEpiBf16Allreduce only) sum the finished tiles over the ranks (namespace ar).
 // Loads use no cluster multicast: every CTA reads its own operands from global memory.
 #pragma once
 
@@ -42,22 +41,12 @@ constexpr int STAGES = 7;
 constexpr int UMMA_K = 16;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-// kEpiBf16Allreduce adds two all-reduce warps (10, 11) and a ring of kArSlots tile records
-// between the epilogue warps and them.
-constexpr int kArWarps = 2;
-constexpr int kArSlots = 4;
-template <int EPI>
-__host__ __device__ constexpr int threads_for() {
-  return EPI == kEpiBf16Allreduce ? kThreads + 32 * kArWarps : kThreads;
-}
 constexpr uint32_t A_STAGE_BYTES = HM * BK * 2;  // 16 KiB
 constexpr uint32_t B_STAGE_BYTES = HN * BK * 2;  // 16 KiB
 constexpr uint32_t STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr uint32_t MN_CHUNK_BYTES = 64 * BK * 2;
 constexpr uint32_t TMEM_COLS = 512;  // two accumulators of 128 lanes x 256 fp32 columns
-// barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, ar_ready[kArSlots],
-// ar_free[kArSlots]; then the TMEM address slot and the ring's region masks
-constexpr uint32_t BAR_BYTES = (2 * STAGES + 5 + 2 * kArSlots) * 8 + 8 + kArSlots * 4;
+constexpr uint32_t BAR_BYTES = (2 * STAGES + 5) * 8 + 8;
 constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
 constexpr uint16_t kPairMask = 0x3;
 
@@ -110,21 +99,18 @@ __device__ __forceinline__ bool wait_ready(const uint32_t* flag, uint64_t limit_
 // ---------------------------------------------------------------- fused all-reduce epilogue
 // kEpiBf16Allreduce: the data-parallel dW GEMM sums its output over the ranks while it runs.
 // Every rank computes the same tiles in the same order (its own partial dW, from its rows of
-// the batch). A region is the 32 rows x 128 columns of a tile that one epilogue warp stores.
-// The epilogue warps store their bf16 partial and hand the tile to the CTA's two all-reduce
-// warps through a ring of kArSlots records (mbarriers ar_ready / ar_free and a mask of the
-// regions each warp wrote): the system-scope fence and the cross-rank waits are off their path.
-// For each tile the all-reduce warps make the stores visible system-wide (fence), add 1 to each
-// region's counter in every rank's copy (multimem.red.release), and then reduce the previous
-// tile's regions: once a region's counter shows all ranks, rank r reduces slice r of it through
-// the NVSwitch (multimem.ld_reduce with fp32 accumulation) and writes the sum into every rank's
-// copy (multimem.st). db (fp32, already summed locally by the pre-pass) is reduced the same way
-// by the first CTA's all-reduce warps before its first tile. Completion: each CTA takes a local
-// ticket after its reductions; the last CTA of a rank adds 1 to the completion counter of every
-// rank and waits until all ranks have arrived, so when the kernel ends on a rank, dW and db hold
-// the sums everywhere. Only that CTA waits at the end, so CTAs of one grid never wait for one
-// another. Counters only grow: launch e (the same on every rank) waits for world * (e + 1).
-// Every wait is bounded.
+// the batch). An epilogue warp owns a region of 32 rows x 128 columns of a tile; after storing
+// its bf16 partial there it adds 1 to the region's counter in every rank's copy
+// (multimem.red.release). Once the counter shows all ranks, rank r's warp reduces slice r of
+// the region through the NVSwitch (multimem.ld_reduce with fp32 accumulation) and writes the
+// sum into every rank's copy (multimem.st). The reduction of a region is deferred by one tile,
+// so the ranks' progress on it has a tile's time to line up. db (fp32, already summed locally
+// by the pre-pass) is reduced the same way by the first CTA before its first tile.
+// Completion: each CTA takes a local ticket after its reductions; the last CTA of a rank adds 1
+// to the completion counter of every rank and waits until all ranks have arrived, so when the
+// kernel ends on a rank, dW and db hold the sums everywhere. Only that CTA waits at the end,
+// so CTAs of one grid never wait for one another. Counters only grow: launch e (the same on
+// every rank) waits for world * (e + 1). Every wait is bounded.
 namespace ar {
 constexpr int kDbFlag = 0;      // db: ranks whose pre-pass output is ready
 constexpr int kDoneFlag = 1;    // ranks whose reductions are all issued
@@ -137,7 +123,17 @@ __device__ __forceinline__ uint32_t target(const gemm::Params& p) {
   return static_cast<uint32_t>(p.ar_world) * (p.ar_epoch + 1u);
 }
 
-// This rank's slice of one region (rows row0.., columns col0..col0+127) once every rank stored
+// After the warp's stores to its region: make them visible system-wide, then count the region.
+__device__ __forceinline__ void signal_region(const gemm::Params& p, uint32_t region, uint32_t lane) {
+  __syncwarp();
+  if (lane == 0) {
+    mm::fence_sys();
+    mm::red_release_add(p.ar_mc_flags + kRegion0 + region, 1u);
+  }
+  __syncwarp();
+}
+
+// This rank's slice of the region (rows row0.., columns col0..col0+127) once every rank stored
 // it: 512 16-byte vectors, slice r of world, up to 8 switch round trips in flight per lane.
 __device__ __forceinline__ void reduce_region(const gemm::Params& p, uint32_t region, int row0, int col0,
                                               uint32_t lane) {
@@ -169,18 +165,10 @@ __device__ __forceinline__ void reduce_region(const gemm::Params& p, uint32_t re
   }
 }
 
-// Region (tile, CTA half `rank`, epilogue warp `ew`): its counter index and first row / column.
-// Epilogue warp ew is warp ew + 2, which reads TMEM lane quarter (ew + 2) & 3 and column half ew >> 2.
-__device__ __forceinline__ void region_coords(int tile, int n_tiles, uint32_t rank, int ew, int& region,
-                                              int& row0, int& col0) {
-  region = tile * kRegionsPerTile + static_cast<int>(rank) * 8 + ew;
-  row0 = (tile / n_tiles) * TM + static_cast<int>(rank) * HM + ((ew + 2) & 3) * 32;
-  col0 = (tile % n_tiles) * TN + (ew >> 2) * 128;
-}
-
-// db: the first CTA's all-reduce warps (thread t of 64) sum this rank's slice of db over the
-// ranks, before its first tile.
-__device__ __forceinline__ void reduce_db(const gemm::Params& p, int t, uint32_t lane) {
+// db: the first CTA's eight epilogue warps (thread t = 32 * warp + lane, 256 threads) sum this
+// rank's slice of db over the ranks, before their first tile.
+__device__ __forceinline__ void reduce_db(const gemm::Params& p, uint32_t ew, uint32_t lane) {
+  const int t = static_cast<int>(ew * 32u + lane);
   if (t == 0) {
     mm::fence_sys();
     mm::red_release_add(p.ar_mc_flags + kDbFlag, 1u);
@@ -193,20 +181,20 @@ __device__ __forceinline__ void reduce_db(const gemm::Params& p, int t, uint32_t
   const int per = (nvec + p.ar_world - 1) / p.ar_world;
   const int v0 = p.ar_rank * per;
   const int v1 = min(nvec, v0 + per);
-  for (int v = v0 + t; v < v1; v += 32 * kArWarps) {
+  for (int v = v0 + t; v < v1; v += 256) {
     float4 x;
     mm::ld_reduce_f32x4(p.ar_mc_db + 4 * v, x);
     mm::st_f32x4(p.ar_mc_db + 4 * v, x);
   }
 }
 
-// End of one CTA's all-reduce warps (both call it).
-__device__ __forceinline__ void finish(const gemm::Params& p, int t, uint32_t lane) {
-  asm volatile("bar.sync 1, 64;" ::: "memory");  // both all-reduce warps' reductions are issued
-  if (t == 0) {
+// End of the epilogue of one CTA (all eight epilogue warps call it).
+__device__ __forceinline__ void finish(const gemm::Params& p, uint32_t ew, uint32_t lane) {
+  asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps' reductions are issued
+  if (ew == 0 && lane == 0) {
     mm::fence_sys();
-    const uint32_t k = atomicAdd(p.ar_flags + kTicket, 1u);
-    if (k == gridDim.x - 1u) {
+    const uint32_t t = atomicAdd(p.ar_flags + kTicket, 1u);
+    if (t == gridDim.x - 1u) {
       p.ar_flags[kTicket] = 0u;  // every CTA of this launch has taken its ticket
       mm::fence_sys();
       mm::red_release_add(p.ar_mc_flags + kDoneFlag, 1u);
@@ -218,7 +206,7 @@ __device__ __forceinline__ void finish(const gemm::Params& p, int t, uint32_t la
 }  // namespace ar
 
 template <bool A_MN, bool B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                  const gemm::Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -232,10 +220,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = bars + 2 * STAGES + 2;
   uint64_t* drain = bars + 2 * STAGES + 4;
-  uint64_t* ar_ready = bars + 2 * STAGES + 5;             // [kArSlots]
-  uint64_t* ar_free = ar_ready + kArSlots;                // [kArSlots]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ar_free + kArSlots);
-  uint32_t* ar_mask = tmem_slot + 2;                      // [kArSlots]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
 
   const uint32_t warp = warp_id_sync();
   const uint32_t lane = lane_id();
@@ -259,13 +244,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       mbar_init(&acc_empty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
-    if constexpr (EPI == kEpiBf16Allreduce) {
-      for (int a = 0; a < kArSlots; ++a) {
-        mbar_init(&ar_ready[a], kEpiWarps);  // the epilogue warps of this CTA
-        mbar_init(&ar_free[a], kArWarps);
-        ar_mask[a] = 0u;
-      }
-    }
     fence_mbarrier_init();
     tma_prefetch_desc(&tma);
     tma_prefetch_desc(&tmb);
@@ -355,55 +333,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       gemm::drain_wait(drain, 0u);
     }
     __syncwarp();
-  } else if (EPI == kEpiBf16Allreduce && warp >= 2 + kEpiWarps) {
-    // ------------------------------------------------------------ all-reduce warps (10, 11)
-    const int aw = static_cast<int>(warp) - 2 - kEpiWarps;  // 0 or 1: epilogue warps 4*aw .. 4*aw+3
-    const int t = aw * 32 + static_cast<int>(lane);
-    if (blockIdx.x == 0) ar::reduce_db(p, t, lane);
-    uint32_t pend_mask = 0u;  // regions of the previous tile this warp reduces (bit = ew - 4*aw)
-    int pend_tile = -1;
-    bool ok = true;
-    Item it;
-    auto reduce_pending = [&]() {
-      for (int r = 0; r < 4; ++r) {
-        if (!((pend_mask >> r) & 1u)) continue;
-        int region, row0, col0;
-        ar::region_coords(pend_tile, n_tiles, rank, 4 * aw + r, region, row0, col0);
-        ar::reduce_region(p, static_cast<uint32_t>(region), row0, col0, lane);
-      }
-    };
-    for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it); ++i) {
-      const int slot = i % kArSlots;
-      const uint32_t par = static_cast<uint32_t>(i / kArSlots) & 1u;
-      if (!mbar_wait(&ar_ready[slot], par, kFaultWaitAccFull)) { ok = false; break; }
-      // regions of this tile that epilogue warps 4*aw .. 4*aw+3 stored on this rank
-      const uint32_t mine = (ar_mask[slot] >> (4 * aw)) & 0xfu;
-      if (lane == 0 && mine != 0u) {
-        mm::fence_sys();  // the epilogue warps' stores, observed through ar_ready, system-wide
-        for (int r = 0; r < 4; ++r) {
-          if (!((mine >> r) & 1u)) continue;
-          int region, row0, col0;
-          ar::region_coords(it.tile, n_tiles, rank, 4 * aw + r, region, row0, col0);
-          mm::red_release_add(p.ar_mc_flags + ar::kRegion0 + region, 1u);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        atomicAnd(&ar_mask[slot], ~(0xfu << (4 * aw)));
-        mbar_arrive(&ar_free[slot]);
-      }
-      reduce_pending();
-      pend_mask = mine;
-      pend_tile = it.tile;
-    }
-    if (ok) reduce_pending();
-    ar::finish(p, t, lane);
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9)
     const uint32_t q = warp & 3u;                 // TMEM lane quarter
     const uint32_t ew = warp - 2u;                // epilogue warp 0..7
     const int c_lo = static_cast<int>(ew >> 2) * (TN / 64);  // first of this warp's 4 chunks
     uint32_t acc = 0, acc_ph = 0;
+    [[maybe_unused]] int pend_region = -1, pend_row = 0, pend_col = 0;
+    if constexpr (EPI == kEpiBf16Allreduce) {
+      if (blockIdx.x == 0) ar::reduce_db(p, ew, lane);
+    }
     Item it;
     for (int i = 0; work_item(i, cluster, num_clusters, num_tiles, p.sk_mode, p.sk_first, k_blocks, it); ++i) {
       const int m0 = (it.tile / n_tiles) * TM + static_cast<int>(rank) * HM;
@@ -474,16 +413,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       acc ^= 1u;
       if (acc == 0u) acc_ph ^= 1u;
       if constexpr (EPI == kEpiBf16Allreduce) {
-        // hand the tile to the all-reduce warps: wait until they released this ring slot,
-        // mark this warp's region if it stored one (a split tile's first half does not),
-        // then arrive (the arrive orders this warp's stores before their system-wide fence)
-        const int slot = i % kArSlots;
-        const uint32_t par = static_cast<uint32_t>(i / kArSlots) & 1u;
-        if (!mbar_wait(&ar_free[slot], par ^ 1u, kFaultWaitAccEmpty)) break;
-        if (lane == 0 && (!split || adder)) atomicOr(&ar_mask[slot], 1u << ew);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ar_ready[slot]);
+        if (!split || adder) {  // this warp stored its region of the tile on this rank
+          const int region = it.tile * ar::kRegionsPerTile + static_cast<int>(rank * 8u + ew);
+          ar::signal_region(p, static_cast<uint32_t>(region), lane);
+          if (pend_region >= 0) ar::reduce_region(p, static_cast<uint32_t>(pend_region), pend_row, pend_col, lane);
+          pend_region = region;
+          pend_row = m0 + static_cast<int>(q * 32u);
+          pend_col = n0 + c_lo * 32;
+        }
       }
+    }
+    if constexpr (EPI == kEpiBf16Allreduce) {
+      if (pend_region >= 0) ar::reduce_region(p, static_cast<uint32_t>(pend_region), pend_row, pend_col, lane);
+      ar::finish(p, ew, lane);
     }
   }
 
