@@ -58,24 +58,23 @@ def _traffic():
 
 
 _SAMPLER_SRC = r"""
-import sys, time
+import signal, sys, time
 import pynvml
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
 interval = float(sys.argv[2])
+stop = [False]
+signal.signal(signal.SIGTERM, lambda *a: stop.__setitem__(0, True))
 print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
 out = []
 deadline = time.monotonic() + float(sys.argv[3])
-while time.monotonic() < deadline:
+while not stop[0] and time.monotonic() < deadline:
     t = time.monotonic()
     try:
         out.append("%.6f %d %d" % (t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
                                    pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
     except Exception:
         pass
-    if len(out) >= 64:
-        print("\n".join(out), flush=True)
-        out = []
     time.sleep(interval)
 print("\n".join(out), flush=True)
 """
@@ -123,10 +122,11 @@ class ClockSampler:
         self.t1 = time.monotonic()
         if self.proc is None:
             return
-        self.proc.kill()
+        self.proc.terminate()  # the sampler prints its samples on SIGTERM, then exits
         try:
-            rest, _ = self.proc.communicate(timeout=10)
+            rest, _ = self.proc.communicate(timeout=20)
         except Exception:
+            self.proc.kill()
             rest = ""
         for ln in rest.splitlines():
             parts = ln.split()
