@@ -25,7 +25,12 @@ namespace c3cu {
 namespace nvls {
 
 constexpr int kThreads = 512;
-constexpr int kUnroll = 8;
+// Switch round trips in flight per thread (multimem.ld_reduce has a long latency: the switch
+// gathers from every GPU).
+#ifndef C3CU_NVLS_UNROLL
+#define C3CU_NVLS_UNROLL 8
+#endif
+constexpr int kUnroll = C3CU_NVLS_UNROLL;
 
 using mm::ld_acquire_sys;
 using mm::ld_reduce_bf16x8;
