@@ -293,10 +293,15 @@ def run_c3(args):
     # dX beside dW: +1.7% at N=1. At N > 1 the default collective overlaps its all-reduce with
     # dX instead (dX after dW, on SMs left free for the all-reduce).
     overlap_dx = os.environ.get("C3_DX_OVERLAP", "1" if world == 1 else "0") == "1"
+    # Split in-switch all-reduce: C3_AR_PEER_FRAC of dW summed from peer loads by C3_AR_PEER_CTAS
+    # of the all-reduce's CTAs, the rest in the switch (0: switch only).
+    peer_frac = float(os.environ.get("C3_AR_PEER_FRAC", "0")) if ar_env == "nvls" else 0.0
+    peer_ctas = int(os.environ.get("C3_AR_PEER_CTAS", "6")) if peer_frac > 0 else 0
     train = LinearReluTrainStep(M, N, K, dev, grad_dtype,
                                 collective="auto" if world == 1 else ar_env,
                                 chunks=chunks, num_ctas=int(os.environ.get("C3_NVLS_CTAS", str(ar_ctas))),
-                                reserve_sms=reserve, overlap_dx=overlap_dx)
+                                reserve_sms=reserve, overlap_dx=overlap_dx, peer_frac=peer_frac,
+                                peer_ctas=peer_ctas)
     chunks = len(train.bands)
     collective = "none" if world == 1 else train.sync.collective
     comp = torch.cuda.current_stream(dev)
@@ -387,6 +392,7 @@ def run_c3(args):
                                         f" dW band ends, overlapped with the rest of dW and dX") if world > 1 else ""),
                        "grad_dtype": {"dW": "bf16" if grad_bf16 else "fp32", "db": "fp32"},
                        "dw_bands": chunks, "sms_reserved_for_allreduce": reserve,
+                       "allreduce_peer_part": {"fraction": peer_frac, "ctas": peer_ctas},
                        "dx_beside_dw": overlap_dx,
                        "programmatic_dependent_launch": bool(launch_overlap),
                        "allreduce": {"fused": "dW GEMM that sums dW and db over the ranks in its epilogue "

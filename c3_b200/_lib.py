@@ -64,6 +64,8 @@ _SIGNATURES = {
     "c3cu_gemm_tune_get": ([_i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_i)], _i),
     "c3cu_gemm_tune_clear": ([], _i),
     "c3cu_nvls_allreduce": ([_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, ctypes.c_uint32, _i, _vp], _i),
+    "c3cu_nvls_allreduce_split": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i, _i, ctypes.c_uint32,
+                                   _i, _i, _vp], _i),
     "c3cu_nccl_version": ([ctypes.POINTER(_i)], _i),
     "c3cu_nccl_unique_id": ([_vp], _i),
     "c3cu_nccl_comm_init": ([ctypes.POINTER(_vp), _vp, _i, _i], _i),

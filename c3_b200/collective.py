@@ -22,6 +22,16 @@ def _align(n: int, a: int = 256) -> int:
     return (n + a - 1) // a * a
 
 
+def split_point(count: int, peer_frac: float) -> int:
+    """First bf16 element of the peer part when the last `peer_frac` of `count` elements (a
+    multiple of 8) go to peer loads: a multiple of 8, count when the fraction rounds to nothing."""
+    if not 0.0 <= peer_frac <= 1.0:
+        raise ValueError(f"peer_frac must be in [0, 1], got {peer_frac}")
+    vecs = count // 8
+    peer_vecs = int(round(vecs * peer_frac))
+    return (vecs - peer_vecs) * 8
+
+
 class NvlsAllReduce:
     def __init__(self, numel: int, device: torch.device, group=None, num_ctas: int = 32,
                  numel_bf16: int = 0, ar_flag_words: int = 0):
@@ -59,6 +69,10 @@ class NvlsAllReduce:
         if int(self.hdl.buffer_size) < offset + nbytes:
             raise RuntimeError("symmetric allocation smaller than the gradient buffer")
         self.mc = mc_base + offset
+        # every rank's copy of this buffer through its unicast address, as mapped in this process
+        # (the split all-reduce reads its slice of the peer part from each of them)
+        self.peer_bases = [int(self.hdl.buffer_ptrs[r]) + offset for r in range(self.world)]
+        self._peer_arr = (ctypes.c_void_p * self.world)(*self.peer_bases)
         self.flag_local = self.buf.data_ptr() + self.flag_off
         self.flag_mc = self.mc + self.flag_off
         self.ar_flags_local = self.buf.data_ptr() + self.ar_flags_off
@@ -98,6 +112,27 @@ class NvlsAllReduce:
                                              self.world, self.epoch, self.num_ctas,
                                              ctypes.c_void_p(s.cuda_stream))
         _lib.check(rc, "c3cu_nvls_allreduce")
+        self.epoch += 1
+
+    def allreduce_split_(self, bf16_range=None, f32_range=None, peer_frac: float = 0.0, peer_ctas: int = 0,
+                         stream: torch.cuda.Stream | None = None):
+        """allreduce2_ with the last `peer_frac` of the bf16 range (rounded to whole 8-element
+        vectors) summed from peer loads by `peer_ctas` of the num_ctas CTAs and the rest in the
+        switch (c3cu_nvls_allreduce_split). peer_frac 0 is allreduce2_."""
+        blo, bhi = bf16_range or (0, 0)
+        flo, fhi = f32_range or (0, 0)
+        count = bhi - blo
+        peer_from = split_point(count, peer_frac)
+        if peer_from == count:
+            self.allreduce2_(bf16_range, f32_range, stream)
+            return
+        s = stream or torch.cuda.current_stream(self.buf.device)
+        rc = _lib.load().c3cu_nvls_allreduce_split(
+            ctypes.c_void_p(self.mc), self._peer_arr, ctypes.c_void_p(self.flag_mc),
+            ctypes.c_void_p(self.flag_local), self.bf16_off + 2 * blo, count, peer_from, self.f32_off + 4 * flo,
+            fhi - flo, self.rank, self.world, self.epoch, self.num_ctas, peer_ctas,
+            ctypes.c_void_p(s.cuda_stream))
+        _lib.check(rc, "c3cu_nvls_allreduce_split")
         self.epoch += 1
 
 

@@ -4,8 +4,8 @@
 //
 // An address passed as `mc` is a multicast address: every rank bound its copy of the buffer to
 // one NVLink multicast object, and an access through the multicast address reaches all copies.
-// Only multimem.* loads, stores and reductions are used here; no TMA or bulk copy touches
-// multicast or peer memory.
+// Besides multimem.* loads, stores and reductions there is one plain 16-byte load through a
+// rank's unicast address (ld_unicast_v4); no TMA or bulk copy touches multicast or peer memory.
 #pragma once
 
 #include "common.cuh"
@@ -55,6 +55,17 @@ __device__ __forceinline__ void red_release_add(uint32_t* mc, uint32_t v) {
 }
 
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// 16 bytes from a rank's own copy of the buffer through its unicast address (this GPU's memory,
+// or a peer's over NVLink). Volatile: never served from a line cached by an earlier launch.
+__device__ __forceinline__ uint4 ld_unicast_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;

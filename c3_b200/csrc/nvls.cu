@@ -14,7 +14,8 @@
 // arrived. The counter only grows: call e (0-based, the same on every rank) waits for
 // world * (2e + 1) and world * (2e + 2).
 //
-// No TMA and no multicast TMA loads are used; only multimem loads/stores/reductions.
+// No TMA and no multicast TMA loads are used; only multimem loads/stores/reductions, and (in
+// the split call) plain 16-byte loads of each rank's copy through its unicast address.
 #include "common.cuh"
 #include "host_util.h"
 #include "multimem.cuh"
@@ -64,15 +65,17 @@ __device__ bool barrier(uint32_t* mc_flag, const uint32_t* local_flag, uint32_t 
 
 // Reduces this rank's slice of a segment of `count` elements at `mc` (16-byte units of
 // kPerVec elements; count must be a multiple of kPerVec).
+// The work is spread over CTAs [0, nctas) of the grid; `cta` is this CTA's index among them.
 template <bool BF16>
-__device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int rank, int world) {
+__device__ __forceinline__ void reduce_segment(uint8_t* mc, int64_t count, int rank, int world, int cta,
+                                               int nctas) {
   constexpr int64_t kPerVec = BF16 ? 8 : 4;
   const int64_t nvec = count / kPerVec;
   const int64_t per = (nvec + world - 1) / world;
   const int64_t v0 = per * rank;
   const int64_t v1 = min(nvec, v0 + per);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t i = v0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(nctas) * blockDim.x;
+  int64_t i = v0 + static_cast<int64_t>(cta) * blockDim.x + threadIdx.x;
   for (; i + stride * (kUnroll - 1) < v1; i += stride * kUnroll) {
     uint4 v[kUnroll];
 #pragma unroll
@@ -118,8 +121,93 @@ __global__ void __launch_bounds__(kThreads)
                       uint32_t epoch) {
   const uint32_t arrivals = static_cast<uint32_t>(world) * gridDim.x;
   if (!barrier(mc_flag, local_flag, arrivals * (2u * epoch + 1u))) return;
-  if (bf16_count > 0) reduce_segment<true>(mc_base + bf16_off, bf16_count, rank, world);
-  if (f32_count > 0) reduce_segment<false>(mc_base + f32_off, f32_count, rank, world);
+  const int cta = static_cast<int>(blockIdx.x), nctas = static_cast<int>(gridDim.x);
+  if (bf16_count > 0) reduce_segment<true>(mc_base + bf16_off, bf16_count, rank, world, cta, nctas);
+  if (f32_count > 0) reduce_segment<false>(mc_base + f32_off, f32_count, rank, world, cta, nctas);
+  barrier(mc_flag, local_flag, arrivals * (2u * epoch + 2u));
+}
+
+// ------------------------------------------------------------------ split: switch + peer loads
+// The switch's reductions alone leave part of the NVLink bandwidth unused: each rank's link
+// carries about one buffer's worth each way in the time the switch takes to reduce it. The split
+// call therefore reduces the tail of the bf16 segment without the switch's arithmetic: a rank
+// reads its slice of that tail from every rank's copy through plain unicast addresses (its own
+// copy from local memory, the others over NVLink), adds the values in fp32 in rank order, rounds
+// once to bf16 and broadcasts the sum with multimem.st, as the switch path does. Both parts run
+// at once on disjoint CTAs between the same two barriers.
+constexpr int kMaxWorld = 8;
+constexpr int kPeerUnroll = 2;  // vectors per thread in flight, each read from every rank
+
+struct PeerBases {
+  const uint8_t* p[kMaxWorld];  // each rank's copy of the buffer (unicast), ranks 0..world-1
+};
+
+// Vectors [vlo, vhi) (16 bytes = 8 bf16 each) of the segment at byte offset `off`: this rank's
+// slice of them, over CTAs [0, nctas) of the peer group.
+__device__ __forceinline__ void peer_segment(uint8_t* mc, const PeerBases& pb, int64_t off, int64_t vlo,
+                                             int64_t vhi, int rank, int world, int cta, int nctas) {
+  const int64_t n = vhi - vlo;
+  const int64_t per = (n + world - 1) / world;
+  const int64_t s0 = vlo + per * rank;
+  const int64_t s1 = min(vhi, s0 + per);
+  const int64_t stride = static_cast<int64_t>(nctas) * blockDim.x;
+  for (int64_t i = s0 + static_cast<int64_t>(cta) * blockDim.x + threadIdx.x; i < s1; i += stride * kPeerUnroll) {
+    uint4 x[kPeerUnroll][kMaxWorld];
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t j = i + stride * u;
+      if (j < s1) {
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+          if (r < world) x[u][r] = mm::ld_unicast_v4(pb.p[r] + off + j * 16);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t j = i + stride * u;
+      if (j >= s1) continue;
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r) {
+        if (r >= world) continue;
+        const uint32_t w[4] = {x[u][r].x, x[u][r].y, x[u][r].z, x[u][r].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          // a 32-bit word holds elements 2q (low half) and 2q + 1 (high half)
+          acc[2 * q] = __fadd_rn(acc[2 * q], __uint_as_float(w[q] << 16));
+          acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], __uint_as_float(w[q] & 0xffff0000u));
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+        o[q] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      st_bf16x8(mc + off + j * 16, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+// CTAs [0, gridDim.x - peer_ctas) reduce bf16 elements [0, peer_from) and the fp32 segment in
+// the switch; the last peer_ctas CTAs reduce bf16 elements [peer_from, bf16_count) by peer loads.
+__global__ void __launch_bounds__(kThreads)
+    allreduce_split_kernel(uint8_t* mc_base, PeerBases pb, uint32_t* mc_flag, const uint32_t* local_flag,
+                           int64_t bf16_off, int64_t bf16_count, int64_t peer_from, int64_t f32_off,
+                           int64_t f32_count, int rank, int world, uint32_t epoch, int peer_ctas) {
+  const uint32_t arrivals = static_cast<uint32_t>(world) * gridDim.x;
+  if (!barrier(mc_flag, local_flag, arrivals * (2u * epoch + 1u))) return;
+  const int switch_ctas = static_cast<int>(gridDim.x) - peer_ctas;
+  const int cta = static_cast<int>(blockIdx.x);
+  if (cta < switch_ctas) {
+    if (peer_from > 0) reduce_segment<true>(mc_base + bf16_off, peer_from, rank, world, cta, switch_ctas);
+    if (f32_count > 0) reduce_segment<false>(mc_base + f32_off, f32_count, rank, world, cta, switch_ctas);
+  } else if (peer_from < bf16_count) {
+    peer_segment(mc_base, pb, bf16_off, peer_from / 8, bf16_count / 8, rank, world, cta - switch_ctas,
+                 peer_ctas);
+  }
   barrier(mc_flag, local_flag, arrivals * (2u * epoch + 2u));
 }
 
@@ -195,6 +283,55 @@ extern "C" int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint3
       static_cast<uint8_t*>(mc_base), mc_flag, local_flag, bf16_offset, bf16_count, f32_offset, f32_count,
       rank, world, epoch);
   return cuda_status(cudaGetLastError(), "nvls_allreduce: launch");
+}
+
+extern "C" int c3cu_nvls_allreduce_split(void* mc_base, const void* const* peer_bases, uint32_t* mc_flag,
+                                         const uint32_t* local_flag, int64_t bf16_offset, int64_t bf16_count,
+                                         int64_t bf16_peer_from, int64_t f32_offset, int64_t f32_count, int rank,
+                                         int world, uint32_t epoch, int num_ctas, int peer_ctas,
+                                         c3cu_stream_t stream) {
+  using namespace c3cu;
+  int rc = require_sm100();
+  if (rc != C3CU_OK) return rc;
+  if (!mc_base || !mc_flag || !local_flag || bf16_offset < 0 || bf16_count < 0 || f32_offset < 0 ||
+      f32_count < 0 || world < 1 || world > nvls::kMaxWorld || rank < 0 || rank >= world || num_ctas < 1 ||
+      num_ctas > 1024 || bf16_peer_from < 0 || bf16_peer_from > bf16_count || peer_ctas < 0 ||
+      peer_ctas > num_ctas) {
+    set_error("nvls_allreduce_split: bad arguments (at most 8 ranks; 0 <= bf16_peer_from <= bf16_count; "
+              "0 <= peer_ctas <= num_ctas)");
+    return C3CU_ERR_INVALID;
+  }
+  const bool peer_part = bf16_peer_from < bf16_count;
+  const bool switch_part = bf16_peer_from > 0 || f32_count > 0;
+  if ((peer_part && peer_ctas < 1) || (switch_part && peer_ctas >= num_ctas) || (!peer_part && peer_ctas != 0)) {
+    set_error("nvls_allreduce_split: peer_ctas must be >= 1 when bf16_peer_from < bf16_count, 0 when it "
+              "equals bf16_count, and leave at least one CTA for the switch part when it is not empty");
+    return C3CU_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(mc_base) & 15u) || (bf16_offset & 15) || (f32_offset & 15) ||
+      (bf16_count % 8) || (bf16_peer_from % 8) || (f32_count % 4)) {
+    set_error("nvls_allreduce_split: segments must start on 16 bytes and hold whole 16-byte vectors "
+              "(bf16 count and bf16_peer_from %% 8, fp32 count %% 4)");
+    return C3CU_ERR_ALIGN;
+  }
+  nvls::PeerBases pb{};
+  if (peer_part) {
+    if (!peer_bases) {
+      set_error("nvls_allreduce_split: peer_bases is NULL");
+      return C3CU_ERR_INVALID;
+    }
+    for (int r = 0; r < world; ++r) {
+      if (!peer_bases[r] || (reinterpret_cast<uintptr_t>(peer_bases[r]) & 15u)) {
+        set_error("nvls_allreduce_split: every rank's base must be a 16-byte-aligned device address");
+        return C3CU_ERR_ALIGN;
+      }
+      pb.p[r] = static_cast<const uint8_t*>(peer_bases[r]);
+    }
+  }
+  nvls::allreduce_split_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(mc_base), pb, mc_flag, local_flag, bf16_offset, bf16_count, bf16_peer_from,
+      f32_offset, f32_count, rank, world, epoch, peer_ctas);
+  return cuda_status(cudaGetLastError(), "nvls_allreduce_split: launch");
 }
 
 extern "C" int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,

@@ -90,7 +90,11 @@ class GradientSync:
     """dW [N, K] (bf16 or fp32) and db [N] (fp32) of one rank, summed over a process group."""
 
     def __init__(self, n: int, k: int, device: torch.device, grad_dtype: torch.dtype = torch.bfloat16,
-                 collective: str = "auto", group=None, num_ctas: int = 16):
+                 collective: str = "auto", group=None, num_ctas: int = 16, peer_frac: float = 0.0,
+                 peer_ctas: int = 0):
+        """`peer_frac` > 0 (bf16 dW, in-switch collective): that fraction of each dW band is summed
+        from peer loads by `peer_ctas` of the `num_ctas` CTAs while the switch sums the rest
+        (c3cu_nvls_allreduce_split)."""
         if grad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError(f"dW dtype must be bfloat16 or float32, got {grad_dtype}")
         if collective not in ("auto", "fused", "nvls", "nccl", "group"):
@@ -100,6 +104,10 @@ class GradientSync:
         self.n, self.k = n, k
         self.device = torch.device(device)
         self.grad_dtype = grad_dtype
+        if not 0.0 <= peer_frac <= 1.0 or peer_ctas < 0 or (peer_frac > 0 and not 1 <= peer_ctas < num_ctas):
+            raise ValueError(f"peer_frac {peer_frac} / peer_ctas {peer_ctas}: need 0 <= peer_frac <= 1 and, "
+                             f"when peer_frac > 0, 1 <= peer_ctas < num_ctas ({num_ctas})")
+        self.peer_frac, self.peer_ctas = peer_frac, peer_ctas
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.nvls = None
@@ -158,8 +166,12 @@ class GradientSync:
         k, n = self.k, self.n
         if self.nvls is not None:
             if self.grad_dtype == torch.bfloat16:
-                self.nvls.allreduce2_((lo * k, hi * k) if hi > lo else None,
-                                      (0, n) if with_db else None, stream)
+                if self.peer_frac > 0 and hi > lo:
+                    self.nvls.allreduce_split_((lo * k, hi * k), (0, n) if with_db else None, self.peer_frac,
+                                               self.peer_ctas, stream)
+                else:
+                    self.nvls.allreduce2_((lo * k, hi * k) if hi > lo else None,
+                                          (0, n) if with_db else None, stream)
             elif with_db and hi == n:
                 self.nvls.allreduce_(lo * k, n * k + n, stream)
             else:
@@ -222,11 +234,11 @@ class LinearReluTrainStep:
 
     def __init__(self, m: int, n: int, k: int, device: torch.device, grad_dtype=torch.bfloat16,
                  collective: str = "auto", group=None, chunks: int = 1, num_ctas: int = 16,
-                 reserve_sms: int = 0, overlap_dx: bool = False):
+                 reserve_sms: int = 0, overlap_dx: bool = False, peer_frac: float = 0.0, peer_ctas: int = 0):
         from . import _lib
         self.m, self.n, self.k = m, n, k
         self.device = torch.device(device)
-        self.sync = GradientSync(n, k, self.device, grad_dtype, collective, group, num_ctas)
+        self.sync = GradientSync(n, k, self.device, grad_dtype, collective, group, num_ctas, peer_frac, peer_ctas)
         self.world = self.sync.world
         self.bands = [(0, n)] if self.sync.fused else dw_bands(n, chunks)
         self.reserve_sms = reserve_sms if self.world > 1 else 0

@@ -308,6 +308,19 @@ int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* l
 int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint32_t* local_flag,
                         int64_t bf16_offset, int64_t bf16_count, int64_t f32_offset, int64_t f32_count,
                         int rank, int world, uint32_t epoch, int num_ctas, c3cu_stream_t stream);
+/* c3cu_nvls_allreduce with the bf16 segment split in two parts that run at once on disjoint
+ * CTAs: elements [0, bf16_peer_from) and the fp32 segment are summed in the switch by
+ * num_ctas - peer_ctas CTAs; elements [bf16_peer_from, bf16_count) by peer_ctas CTAs that read
+ * their rank's slice from every rank's copy through its unicast address, add in fp32 in rank
+ * order, round once to bf16 and broadcast with multimem.st. peer_bases is a host array of
+ * `world` (at most 8) 16-byte-aligned device addresses: rank r's copy of the buffer as mapped in
+ * this process (its own copy at [rank]). bf16_peer_from is a multiple of 8; peer_ctas is 0 when
+ * the peer part is empty and otherwise leaves at least one CTA for a non-empty switch part.
+ * Same barrier counter and epoch sequence as c3cu_nvls_allreduce (one epoch per call). */
+int c3cu_nvls_allreduce_split(void* mc_base, const void* const* peer_bases, uint32_t* mc_flag,
+                              const uint32_t* local_flag, int64_t bf16_offset, int64_t bf16_count,
+                              int64_t bf16_peer_from, int64_t f32_offset, int64_t f32_count, int rank,
+                              int world, uint32_t epoch, int num_ctas, int peer_ctas, c3cu_stream_t stream);
 
 /* ------------------------------------------------------------------ training step (cfg1)
  * Softmax cross-entropy over C classes, mean over B rows, fp32, one kernel:

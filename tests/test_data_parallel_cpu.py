@@ -298,3 +298,25 @@ def test_dw_bands_properties(n, chunks):
         assert a1 == b0
     if len(bands) > 1:
         assert all((hi - lo) % 8 == 0 for lo, hi in bands) and len(bands) == chunks
+
+
+@given(st.integers(0, 1 << 20).map(lambda v: v * 8), st.floats(0.0, 1.0))
+@settings(max_examples=200, deadline=None)
+def test_split_point_properties(count, frac):
+    """The switch / peer boundary of the split all-reduce: whole 8-element vectors, the peer part
+    within half a vector of the asked fraction, and the whole range at the ends."""
+    from c3_b200.collective import split_point
+    p = split_point(count, frac)
+    assert p % 8 == 0 and 0 <= p <= count
+    assert abs((count - p) - frac * count) <= 4
+    assert split_point(count, 0.0) == count and split_point(count, 1.0) == 0
+
+
+def test_split_options_are_checked():
+    from c3_b200.collective import split_point
+    from c3_b200.data_parallel import GradientSync
+    with pytest.raises(ValueError):
+        split_point(64, 1.5)
+    for frac, ctas in ((0.3, 0), (0.3, 16), (-0.1, 1), (1.2, 1)):
+        with pytest.raises(ValueError, match="peer_frac"):
+            GradientSync(64, 64, "cpu", collective="group", num_ctas=16, peer_frac=frac, peer_ctas=ctas)

@@ -72,6 +72,36 @@ def _worker(rank, world, port, q):
             print(f"rank {rank} bf16 max err/|sum| = {float((err_b / ref_b.abs().clamp_min(1e-3)).max()):.3e}",
                   flush=True)
             results[f"f32_{trial}"] = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max())
+        # split call (c3cu_nvls_allreduce_split): the peer part is an fp32 sum in rank order
+        # rounded once to nearest, so with two ranks (an exact fp32 sum of two bf16 values) it
+        # equals NCCL's fp32 sum rounded to bf16 bit for bit; the switch part as above
+        from c3_b200.collective import split_point
+        for trial, (frac, pctas, lo, hi, with_f32) in enumerate(
+                [(0.3, 3, 0, nb, True), (0.5, 1, 8 * 1001, nb - 8 * 77, False), (1.0, 7, 0, nb, True),
+                 (1.0, 8, 8, 8 * 5003, False)]):
+            g = torch.Generator(device=dev).manual_seed(500 + 10 * trial + rank)
+            xb = torch.randn(nb, generator=g, device=dev).to(torch.bfloat16)
+            xf = torch.randn(nf, generator=g, device=dev)
+            arb.bf16.copy_(xb)
+            arb.f32.copy_(xf)
+            ref_b = xb.float()
+            ref_f = xf.clone()
+            dist.all_reduce(ref_b)
+            dist.all_reduce(ref_f)
+            arb.allreduce_split_((lo, hi), (0, nf) if with_f32 else None, frac, pctas)
+            torch.cuda.synchronize()
+            got = arb.bf16.float()
+            pf = lo + split_point(hi - lo, frac)
+            sw = slice(lo, pf)
+            err_sw = (got[sw] - ref_b[sw]).abs()
+            ok_sw = bool((err_sw <= 2.0 ** -7 * ref_b[sw].abs() + 1e-6).all())
+            peer_exact = torch.equal(arb.bf16[pf:hi], ref_b[pf:hi].to(torch.bfloat16))
+            untouched = torch.equal(arb.bf16[:lo], xb[:lo]) and torch.equal(arb.bf16[hi:], xb[hi:])
+            results[f"split_{trial}"] = 0.0 if (ok_sw and peer_exact and untouched) else \
+                float(1 + (not ok_sw) + 2 * (not peer_exact) + 4 * (not untouched))
+            f_err = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max()) if with_f32 else \
+                float((arb.f32 - xf).abs().max())
+            results[f"split_f32_{trial}"] = f_err
         # NCCL through the C ABI (c3cu_allreduce_grads) against torch's all_reduce
         from c3_b200.collective import NcclComm
         nc = NcclComm(dev)
