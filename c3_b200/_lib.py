@@ -57,6 +57,7 @@ _SIGNATURES = {
     "c3cu_matmul_colsum_f32": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp], _i),
     "c3cu_convert": ([_vp, _i, _vp, _i, _i64, _vp], _i),
     "c3cu_set_gemm_max_ctas": ([_i], _i),
+    "c3cu_set_collective_cluster": ([_i], _i),
     "c3cu_set_gemm_variant": ([_i], _i),
     "c3cu_set_split_wait_ns": ([ctypes.c_uint64], _i),
     "c3cu_set_launch_overlap": ([_i], _i),

@@ -16,6 +16,9 @@
 //
 // No TMA and no multicast TMA loads are used; only multimem loads/stores/reductions, and (in
 // the split call) plain 16-byte loads of each rank's copy through its unicast address.
+#include <atomic>
+#include <utility>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "multimem.cuh"
@@ -32,6 +35,31 @@ constexpr int kThreads = 512;
 #define C3CU_NVLS_UNROLL 8
 #endif
 constexpr int kUnroll = C3CU_NVLS_UNROLL;
+
+// CTAs per thread-block cluster of the all-reduce launches (c3cu_set_collective_cluster): 1, or
+// 2 so that each pair of CTAs takes both SMs of one TPC and leaves whole TPCs to a CTA-pair GEMM
+// running beside it.
+std::atomic<int> g_cluster{1};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ar(void (*kern)(KArgs...), int num_ctas, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_ctas));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  const int cl = g_cluster.load(std::memory_order_relaxed);
+  if (cl > 1 && num_ctas % cl == 0) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 using mm::ld_acquire_sys;
 using mm::ld_reduce_bf16x8;
@@ -279,10 +307,10 @@ extern "C" int c3cu_nvls_allreduce(void* mc_base, uint32_t* mc_flag, const uint3
               "(bf16 count %% 8, fp32 count %% 4)");
     return C3CU_ERR_ALIGN;
   }
-  nvls::allreduce2_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(mc_base), mc_flag, local_flag, bf16_offset, bf16_count, f32_offset, f32_count,
-      rank, world, epoch);
-  return cuda_status(cudaGetLastError(), "nvls_allreduce: launch");
+  return cuda_status(nvls::launch_ar(nvls::allreduce2_kernel, num_ctas, static_cast<cudaStream_t>(stream),
+                                     static_cast<uint8_t*>(mc_base), mc_flag, local_flag, bf16_offset, bf16_count,
+                                     f32_offset, f32_count, rank, world, epoch),
+                     "nvls_allreduce: launch");
 }
 
 extern "C" int c3cu_nvls_allreduce_split(void* mc_base, const void* const* peer_bases, uint32_t* mc_flag,
@@ -328,10 +356,11 @@ extern "C" int c3cu_nvls_allreduce_split(void* mc_base, const void* const* peer_
       pb.p[r] = static_cast<const uint8_t*>(peer_bases[r]);
     }
   }
-  nvls::allreduce_split_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(mc_base), pb, mc_flag, local_flag, bf16_offset, bf16_count, bf16_peer_from,
-      f32_offset, f32_count, rank, world, epoch, peer_ctas);
-  return cuda_status(cudaGetLastError(), "nvls_allreduce_split: launch");
+  return cuda_status(nvls::launch_ar(nvls::allreduce_split_kernel, num_ctas, static_cast<cudaStream_t>(stream),
+                                     static_cast<uint8_t*>(mc_base), pb, mc_flag, local_flag, bf16_offset,
+                                     bf16_count, bf16_peer_from, f32_offset, f32_count, rank, world, epoch,
+                                     peer_ctas),
+                     "nvls_allreduce_split: launch");
 }
 
 extern "C" int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const uint32_t* local_flag,
@@ -349,7 +378,16 @@ extern "C" int c3cu_nvls_allreduce_f32(float* mc_data, uint32_t* mc_flag, const 
     set_error("nvls_allreduce_f32: multicast base must be 16-byte aligned");
     return C3CU_ERR_ALIGN;
   }
-  nvls::allreduce_kernel<<<num_ctas, nvls::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      mc_data, mc_flag, local_flag, lo, hi, rank, world, epoch);
-  return cuda_status(cudaGetLastError(), "nvls_allreduce_f32: launch");
+  return cuda_status(nvls::launch_ar(nvls::allreduce_kernel, num_ctas, static_cast<cudaStream_t>(stream), mc_data,
+                                     mc_flag, local_flag, lo, hi, rank, world, epoch),
+                     "nvls_allreduce_f32: launch");
+}
+
+extern "C" int c3cu_set_collective_cluster(int ctas_per_cluster) {
+  if (ctas_per_cluster != 1 && ctas_per_cluster != 2) {
+    c3cu::set_error("set_collective_cluster: 1 or 2 CTAs per cluster");
+    return C3CU_ERR_INVALID;
+  }
+  c3cu::nvls::g_cluster.store(ctas_per_cluster, std::memory_order_relaxed);
+  return C3CU_OK;
 }

@@ -326,8 +326,15 @@ class LinearReluTrainStep:
             mark("dw")
             mark("dx"); linear.grad_input(self.dZ, W, "nk", self.dX); mark("dx")
             return events() if record else None
+        lib = _lib.load() if self.reserve_sms else None
         for i, (r0, r1) in enumerate(self.bands):
+            # from the second band on, an earlier band's all-reduce runs beside this GEMM: leave
+            # it its SMs, as for dX
+            if lib is not None and i > 0:
+                lib.c3cu_set_gemm_max_ctas(self._sms - self.reserve_sms)
             linear.gemm(self.dZ[:, r0:r1], X, True, True, self.epi, self.dW[r0:r1], M=r1 - r0, N=k, K=m)
+            if lib is not None and i > 0:
+                lib.c3cu_set_gemm_max_ctas(0)
             if self.world > 1:
                 self._ev_band[i].record(comp)
                 self.comm.wait_event(self._ev_band[i])
@@ -342,7 +349,6 @@ class LinearReluTrainStep:
         mark("dw")
         if self.world > 1:
             self._ev_done.record(self.comm)
-        lib = _lib.load() if self.reserve_sms else None
         if lib is not None:
             lib.c3cu_set_gemm_max_ctas(self._sms - self.reserve_sms)
         mark("dx"); linear.grad_input(self.dZ, W, "nk", self.dX); mark("dx")

@@ -130,6 +130,10 @@ int c3cu_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
  * on (0 = one per SM, the default). A host that overlaps a collective with a GEMM lowers it
  * around that launch to leave SMs free; GEMMs launched by other threads are not affected. */
 int c3cu_set_gemm_max_ctas(int max_ctas);
+/* CTAs per thread-block cluster of the in-switch all-reduce launches that follow (process-wide):
+ * 1 (the default) or 2. With 2 (and an even num_ctas) each pair of CTAs runs on the two SMs of
+ * one TPC, so a CTA-pair GEMM running beside the all-reduce keeps whole TPCs. */
+int c3cu_set_collective_cluster(int ctas_per_cluster);
 /* GEMM kernel variant for the calls that follow (process-wide): 0 = automatic (the CTA-pair
  * kernel, 256 x 256 tiles on two SMs with cta_group::2, whenever M > 128, else the single-CTA
  * 128 x 256 kernel; when the last wave of tiles would leave half of the SM pairs idle, its

@@ -28,6 +28,17 @@ def test_version_and_status_calls_without_gpu():
     assert rc == -5
 
 
+def test_collective_cluster_setter_checks_its_value():
+    lib = _lib.load()
+    try:
+        assert lib.c3cu_set_collective_cluster(2) == 0
+        assert lib.c3cu_set_collective_cluster(3) == -1
+        assert "1 or 2" in _lib.last_error()
+        assert lib.c3cu_set_collective_cluster(0) == -1
+    finally:
+        assert lib.c3cu_set_collective_cluster(1) == 0
+
+
 def test_workspace_size_queries_are_pure_host():
     lib = _lib.load()
     assert lib.c3cu_relu_mask_db_workspace(16384, 4096) >= 32 * 4096 * 4
