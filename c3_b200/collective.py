@@ -91,6 +91,8 @@ class NvlsAllReduce:
     def allreduce_(self, lo: int = 0, hi: int | None = None, stream: torch.cuda.Stream | None = None):
         """Sum fp32 elements [lo, hi) of the fp32 region over all ranks (any alignment)."""
         hi = self.numel if hi is None else hi
+        if not 0 <= lo <= hi <= self.numel:
+            raise ValueError(f"fp32 range [{lo}, {hi}) must lie in [0, {self.numel})")
         s = stream or torch.cuda.current_stream(self.buf.device)
         rc = _lib.load().c3cu_nvls_allreduce_f32(ctypes.c_void_p(self.mc + self.f32_off),
                                                  ctypes.c_void_p(self.flag_mc),
@@ -100,11 +102,23 @@ class NvlsAllReduce:
         _lib.check(rc, "c3cu_nvls_allreduce_f32")
         self.epoch += 1
 
+    def _ranges(self, bf16_range, f32_range):
+        """Element ranges of the two regions, checked against the regions' sizes (the kernels take
+        bare offsets, so a range past a region would reach into the rest of the buffer or past it)."""
+        blo, bhi = bf16_range or (0, 0)
+        flo, fhi = f32_range or (0, 0)
+        if not (0 <= blo <= bhi <= self.numel_bf16 and blo % 8 == 0 and bhi % 8 == 0):
+            raise ValueError(f"bf16 range [{blo}, {bhi}) must lie in [0, {self.numel_bf16}) with both ends "
+                             "multiples of 8")
+        if not (0 <= flo <= fhi <= self.numel and flo % 4 == 0 and fhi % 4 == 0):
+            raise ValueError(f"fp32 range [{flo}, {fhi}) must lie in [0, {self.numel}) with both ends "
+                             "multiples of 4")
+        return blo, bhi, flo, fhi
+
     def allreduce2_(self, bf16_range=None, f32_range=None, stream: torch.cuda.Stream | None = None):
         """One call summing bf16 elements [lo, hi) (lo, hi multiples of 8) and fp32 elements
         [lo, hi) (multiples of 4) of the two regions."""
-        blo, bhi = bf16_range or (0, 0)
-        flo, fhi = f32_range or (0, 0)
+        blo, bhi, flo, fhi = self._ranges(bf16_range, f32_range)
         s = stream or torch.cuda.current_stream(self.buf.device)
         rc = _lib.load().c3cu_nvls_allreduce(ctypes.c_void_p(self.mc), ctypes.c_void_p(self.flag_mc),
                                              ctypes.c_void_p(self.flag_local), self.bf16_off + 2 * blo,
@@ -119,8 +133,7 @@ class NvlsAllReduce:
         """allreduce2_ with the last `peer_frac` of the bf16 range (rounded to whole 8-element
         vectors) summed from peer loads by `peer_ctas` of the num_ctas CTAs and the rest in the
         switch (c3cu_nvls_allreduce_split). peer_frac 0 is allreduce2_."""
-        blo, bhi = bf16_range or (0, 0)
-        flo, fhi = f32_range or (0, 0)
+        blo, bhi, flo, fhi = self._ranges(bf16_range, f32_range)
         count = bhi - blo
         peer_from = split_point(count, peer_frac)
         if peer_from == count:

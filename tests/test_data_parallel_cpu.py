@@ -320,3 +320,19 @@ def test_split_options_are_checked():
     for frac, ctas in ((0.3, 0), (0.3, 16), (-0.1, 1), (1.2, 1)):
         with pytest.raises(ValueError, match="peer_frac"):
             GradientSync(64, 64, "cpu", collective="group", num_ctas=16, peer_frac=frac, peer_ctas=ctas)
+
+
+def test_nvls_ranges_are_checked_against_the_regions():
+    """The in-switch all-reduce calls take bare offsets; a range outside its region is refused
+    on the host (no buffer is needed to check it)."""
+    from c3_b200.collective import NvlsAllReduce
+    ar = object.__new__(NvlsAllReduce)
+    ar.numel, ar.numel_bf16 = 100, 64
+    assert ar._ranges((8, 64), (0, 100)) == (8, 64, 0, 100)
+    assert ar._ranges(None, None) == (0, 0, 0, 0)
+    for bad in ((0, 72), (4, 64), (16, 8), (-8, 8)):
+        with pytest.raises(ValueError, match="bf16 range"):
+            ar._ranges(bad, None)
+    for bad in ((0, 104), (2, 8), (8, 4)):
+        with pytest.raises(ValueError, match="fp32 range"):
+            ar._ranges(None, bad)
