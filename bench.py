@@ -6,10 +6,18 @@ Y = relu(X W^T + b) at global batch M=16384, N=K=4096, bf16 operands, fp32 accum
   forward  Y, mask = c3cu_linear_bias_relu_fwd(X, W, b)
   backward dZ, db  = c3cu_relu_mask_db(dY, mask); dW = dZ^T X; dX = dZ W
   N > 1    rows of X / dY are sharded across ranks (strong scaling at fixed global batch);
-           dW (bf16) and db (fp32) are summed over the ranks by the dW GEMM itself (each tile
-           reduced in the NVSwitch as soon as every rank has computed it; C3_ALLREDUCE=nvls
-           runs the separate in-switch all-reduce overlapped with dX instead), and checked after
-           the timed region against an NCCL all-reduce of each rank's partials (allreduce_check).
+           dW (bf16) and db (fp32) are summed over the ranks by the in-switch all-reduce kernel
+           (multimem.ld_reduce / multimem.st) on a side stream, overlapped with dX, and checked
+           after the timed region against an NCCL all-reduce of each rank's partials
+           (allreduce_check).
+  Options (environment; the defaults are the measured best):
+    C3_ALLREDUCE     nvls (default) | fused (the dW GEMM sums its own tiles over the ranks) |
+                     nccl | group
+    C3_NVLS_CTAS, C3_BENCH_AR_SMS   CTAs of the all-reduce / SMs left free for it (20 / 20)
+    C3_BENCH_DW_CHUNKS              dW in row bands, each band's sum started when it is done (1)
+    C3_AR_PEER_FRAC, C3_AR_PEER_CTAS  part of dW summed from peer loads beside the switch (0)
+    C3_DX_OVERLAP    dX beside dW (1 at N = 1, 0 at N > 1);  C3_GRAD_DTYPE bf16 | fp32
+    C3_LAUNCH_OVERLAP  programmatic dependent launch (0);  C3_GEMM_VARIANT (0 = automatic)
   N = 1    after the headline, the other BASELINE configs are measured in the same process
            (configs: cfg2 forward, cfg4 chain, cfg5 FlashAttention, cfg1 MLP step), each with
            its roofline fraction, a CPU baseline and a sampled parity check against the oracle.
