@@ -105,32 +105,6 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 }  // namespace
 
-int encode_2d_plain(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
-                    uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
-  if (!aligned16(base) || (ld * elem_bytes) % 16u != 0u || ld < cols || (box_cols * elem_bytes) % 16u != 0u) {
-    set_error("TMA operand: base %p, row stride %llu x %u bytes or box row %u x %u bytes breaks the 16-byte rule",
-              base, (unsigned long long)ld, elem_bytes, box_cols, elem_bytes);
-    return C3CU_ERR_ALIGN;
-  }
-  auto fn = get_encode_fn();
-  if (!fn) {
-    set_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
-    return C3CU_ERR_CUDA;
-  }
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {ld * elem_bytes};
-  const cuuint32_t box[2] = {box_cols, box_rows};
-  const cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (CUresult %d) rows=%llu cols=%llu ld=%llu box=%ux%u", (int)r,
-              (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)ld, box_cols, box_rows);
-    return C3CU_ERR_CUDA;
-  }
-  return C3CU_OK;
-}
-
 int encode_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                          uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
   if (!aligned16(base)) {

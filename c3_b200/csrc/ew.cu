@@ -10,8 +10,6 @@
 // explicit round-to-nearest intrinsics (__fadd_rn, __fmul_rn, ...) so that the compiler
 // cannot contract them into FMAs: the reference evaluates each node as a separate fp32
 // operation (src/C3/MLIRKernelGen.cpp:394-768), and the kernels keep that order.
-#include <algorithm>
-#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -220,143 +218,6 @@ int64_t colsum_rows_per_block(int64_t M, int64_t N) {
   return rows;
 }
 
-// ------------------------------------------------------------------ pre-pass fed by TMA
-// The same pre-pass (dZ = float(mask) * dY, db = column sums; same summation order within a
-// block) with the loads taken off the consumer threads: a producer warp streams tiles of 32
-// rows x 256 columns of dY (16 KiB) and the matching 32 x 8 mask words (1 KiB) into a ring of
-// shared-memory stages with 2-D TMA copies, so each SM keeps ~150 KB of reads in flight
-// without holding them in registers. The 8 consumer warps read their rows from shared memory,
-// store dZ with 16-byte stores and accumulate as colsum_kernel does. Used when N is a multiple
-// of 128 (the mask's row stride then meets the TMA 16-byte rule) and the pointers are 16-byte
-// aligned; C3CU_PREPASS_TMA=0 at build time keeps colsum_kernel for every shape.
-#ifndef C3CU_PREPASS_TMA
-#define C3CU_PREPASS_TMA 1
-#endif
-constexpr int kTmaRows = 32;
-constexpr int kTmaStages = 3;
-constexpr uint32_t kTmaDyBytes = kTmaRows * kColsPerWarp * 2;       // 16 KiB
-constexpr uint32_t kTmaMaskBytes = kTmaRows * (kColsPerWarp / 32) * 4;  // 1 KiB
-constexpr uint32_t kTmaStageBytes = kTmaDyBytes + kTmaMaskBytes;
-constexpr int kTmaThreads = (kWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
-constexpr int kTmaBlocksPerSm = 3;
-constexpr uint32_t kTmaSmemBytes = kTmaStages * kTmaStageBytes + 2 * kTmaStages * 8 + 128;
-
-__global__ void __launch_bounds__(kTmaThreads)
-    colsum_tma_kernel(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_mask,
-                      __nv_bfloat16* __restrict__ dz, float* __restrict__ out, int M, int N, int rows_per_block,
-                      float* __restrict__ partials, unsigned int* __restrict__ tickets) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                             ~static_cast<uintptr_t>(127));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTmaStages * kTmaStageBytes);
-  uint64_t* empty = full + kTmaStages;
-  __shared__ float red[kWarps][kColsPerWarp];
-  __shared__ bool is_last;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int strip = blockIdx.x;
-  const int rb = blockIdx.y;
-  const int row0 = rb * rows_per_block;
-  const int row1 = min(M, row0 + rows_per_block);
-  const int nchunks = (row1 - row0 + kTmaRows - 1) / kTmaRows;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kTmaStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kWarps);
-    }
-    fence_mbarrier_init();
-  }
-  __syncthreads();
-  pdl_wait();  // the previous kernel on the stream has completed (no-op without PDL)
-  pdl_launch_dependents();
-
-  float acc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-  if (warp == kWarps) {
-    // producer: one lane issues the copies of chunk c into stage c % kTmaStages once the
-    // consumers have released that stage's previous chunk
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_dy);
-      tma_prefetch_desc(&tm_mask);
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kTmaStages;
-        if (c >= kTmaStages && !mbar_wait(&empty[s], ((c / kTmaStages) - 1) & 1u, kFaultWaitEmpty)) break;
-        uint8_t* st = smem + s * kTmaStageBytes;
-        mbar_arrive_expect_tx(&full[s], kTmaStageBytes);
-        tma_load_2d(st, &tm_dy, &full[s], strip * kColsPerWarp, row0 + c * kTmaRows);
-        tma_load_2d(st + kTmaDyBytes, &tm_mask, &full[s], strip * (kColsPerWarp / 32), row0 + c * kTmaRows);
-        issued = c + 1;
-      }
-      // Every copy must have landed before the block's shared memory is released. In the
-      // normal course the consumers already waited for all of them; this matters only after
-      // a recorded fault made them stop early.
-      for (int c = max(0, issued - kTmaStages); c < issued; ++c)
-        if (!mbar_wait(&full[c % kTmaStages], (c / kTmaStages) & 1u, kFaultDrain)) break;
-    }
-  } else {
-    const int col = strip * kColsPerWarp + lane * 8;
-    for (int c = 0; c < nchunks; ++c) {
-      const int s = c % kTmaStages;
-      if (!mbar_wait(&full[s], (c / kTmaStages) & 1u, kFaultWaitFull)) break;
-      const uint8_t* st = smem + s * kTmaStageBytes;
-#pragma unroll
-      for (int i = 0; i < kTmaRows / kWarps; ++i) {
-        const int lr = warp + i * kWarps;  // rows ascend per warp, as in colsum_kernel
-        const int r = row0 + c * kTmaRows + lr;
-        const uint4 q = *reinterpret_cast<const uint4*>(st + lr * (kColsPerWarp * 2) + lane * 16);
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(st + kTmaDyBytes + lr * (kColsPerWarp / 8) +
-                                                               (lane >> 2) * 4);
-        const uint32_t raw[8] = {q.x, q.y, q.z, q.w, 0u, 0u, 0u, 0u};
-        if (r < row1 && col < N) colsum_consume<true>(dz, r, col, N, true, raw, w >> ((lane & 3) * 8), acc);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[j];
-  }
-  __syncthreads();
-  // thread t < 256 adds column t of the strip over the 8 warps, in warp order
-  const int t = threadIdx.x;
-  const int c = strip * kColsPerWarp + t;
-  if (t < kColsPerWarp) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, red[w][t]);
-    if (c < N) partials[(int64_t)rb * N + c] = s;
-    __threadfence();
-  }
-  __syncthreads();
-  if (t == 0) {
-    const unsigned int ticket = atomicAdd(&tickets[strip], 1u);
-    is_last = (ticket == gridDim.y - 1);
-  }
-  __syncthreads();
-  if (is_last && t < kColsPerWarp) {
-    __threadfence();
-    if (c < N) {
-      float tot = 0.f;
-      for (int b = 0; b < static_cast<int>(gridDim.y); ++b)
-        tot = __fadd_rn(tot, __ldcg(partials + (int64_t)b * N + c));
-      out[c] = tot;
-    }
-    if (t == 0) tickets[strip] = 0u;  // re-arm for the next launch on this workspace
-  }
-}
-
-// Rows per block of the TMA pre-pass: one wave of kTmaBlocksPerSm blocks per SM, a multiple of
-// the 32-row tile, and never fewer than colsum_rows_per_block gives (so that the partial sums
-// fit the workspace colsum_workspace sizes).
-int64_t colsum_tma_rows_per_block(int64_t M, int64_t N, int sms) {
-  const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
-  const int64_t target_blocks = static_cast<int64_t>(kTmaBlocksPerSm) * sms;
-  int64_t rows = (M * strips + target_blocks - 1) / target_blocks;
-  rows = (rows + kTmaRows - 1) / kTmaRows * kTmaRows;
-  return std::max(rows, colsum_rows_per_block(M, N));
-}
-
 size_t colsum_workspace(int64_t M, int64_t N) {
   const int64_t rbs = (M + colsum_rows_per_block(M, N) - 1) / colsum_rows_per_block(M, N);
   const int64_t strips = (N + kColsPerWarp - 1) / kColsPerWarp;
@@ -442,28 +303,6 @@ int launch_colsum(const void* in, const uint32_t* mask, void* dz, float* out, in
   const int esize = MASKED ? 2 : 4;
   const int vec_ok = aligned16(in) && (!MASKED || aligned16(dz)) && ((N * esize) % 16 == 0);
   const int ldm = static_cast<int>((N + 31) / 32);
-  if constexpr (MASKED) {
-    if (C3CU_PREPASS_TMA && N % 128 == 0 && aligned16(in) && aligned16(dz) && aligned16(mask)) {
-      const int64_t trpb = colsum_tma_rows_per_block(M, N, sm_count());
-      const int64_t trbs = (M + trpb - 1) / trpb;
-      CUtensorMap tm_dy, tm_mask;
-      rc = encode_2d_plain(&tm_dy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in, static_cast<uint64_t>(M),
-                           static_cast<uint64_t>(N), static_cast<uint64_t>(N), kColsPerWarp, kTmaRows);
-      if (rc != C3CU_OK) return rc;
-      rc = encode_2d_plain(&tm_mask, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, mask, static_cast<uint64_t>(M),
-                           static_cast<uint64_t>(ldm), static_cast<uint64_t>(ldm), kColsPerWarp / 32, kTmaRows);
-      if (rc != C3CU_OK) return rc;
-      static std::atomic<uint64_t> smem_set{0};  // one bit per device
-      rc = set_max_dynamic_smem(reinterpret_cast<const void*>(colsum_tma_kernel), kTmaSmemBytes, smem_set,
-                                "column sum: set max dynamic shared memory");
-      if (rc != C3CU_OK) return rc;
-      dim3 tgrid(static_cast<unsigned>(strips), static_cast<unsigned>(trbs));
-      return cuda_status(launch_kernel(colsum_tma_kernel, tgrid, dim3(kTmaThreads), kTmaSmemBytes, st, tm_dy,
-                                       tm_mask, static_cast<__nv_bfloat16*>(dz), out, static_cast<int>(M),
-                                       static_cast<int>(N), static_cast<int>(trpb), partials, tickets),
-                         "column sum: launch");
-    }
-  }
   dim3 grid(static_cast<unsigned>(strips), static_cast<unsigned>(rbs));
   return cuda_status(launch_kernel(colsum_kernel<MASKED>, grid, dim3(kWarps * 32), 0, st, in, mask,
                                    static_cast<__nv_bfloat16*>(dz), out, static_cast<int>(M),

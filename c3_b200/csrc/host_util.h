@@ -40,12 +40,6 @@ int require_sm100();
 int encode_bf16_2d_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                          uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
-// The same without swizzle, for any element type (elem_bytes per element; rows of `ld`
-// elements): boxes land in shared memory row after row, box_cols * elem_bytes bytes each.
-// Out-of-range parts of a box are filled with zeros.
-int encode_2d_plain(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
-                    uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows);
-
 // Called by c3cu_fault_status when a kernel recorded a fault: a split-K GEMM whose adder gave
 // up waiting may leave its ticket and ready words non-zero (its partner publishes after the
 // adder has reset them), so every pooled split workspace is cleared again on its stream before
