@@ -429,20 +429,7 @@ def run_c3(args):
             # roofline fraction against the clock the kernels ran at
             line["kernel_kcycles"] = {k: ktime[k] * clocks["sm_mhz"] for k in ("fwd", "dw", "dx")}
         if world > 1:
-            phases = {k: ktime[k] for k in kinds}
-            if "dwdx" in ktime:  # dW and dX overlap: count their span once
-                phases = {"fwd": ktime["fwd"], "prepass": ktime["prepass"], "dwdx": ktime["dwdx"]}
-            exposed = max(0.0, ms_per_step - sum(phases.values()))
-            phases["allreduce_exposed"] = exposed
-            # dX runs beside the all-reduce: of the two, the one that ends later sets the step's
-            # tail, whichever of the phases' own durations is larger
-            segments = {k: v for k, v in phases.items() if k != "allreduce_exposed"}
-            ar_total = ktime.get("allreduce") or 0.0
-            if "dx" in segments and ar_total > segments["dx"]:
-                del segments["dx"]
-                segments["allreduce"] = ar_total
-            line["critical_path"] = {"ms": phases, "limiting": max(segments, key=segments.get),
-                                     "allreduce_total_ms": ktime.get("allreduce")}
+            line["critical_path"] = critical_path(ktime, kinds, ms_per_step)
             line["allreduce_check"] = ar_check
         if e2e is not None:
             line["e2e"] = e2e
@@ -469,6 +456,23 @@ def run_c3(args):
               file=sys.stderr)
         return 1
     return 0
+
+
+def critical_path(ktime: dict, kinds, ms_per_step: float) -> dict:
+    """Per-phase device times of one data-parallel step (ms, from kernel_ms), the all-reduce time
+    not hidden behind them, and the phase that limits the step. dX runs beside the all-reduce, so
+    of the two the one that ends later sets the step's tail, whichever of the phases' own
+    durations is larger."""
+    phases = {k: ktime[k] for k in kinds}
+    if "dwdx" in ktime:  # dW and dX overlap: count their span once
+        phases = {"fwd": ktime["fwd"], "prepass": ktime["prepass"], "dwdx": ktime["dwdx"]}
+    phases["allreduce_exposed"] = max(0.0, ms_per_step - sum(phases.values()))
+    segments = {k: v for k, v in phases.items() if k != "allreduce_exposed"}
+    ar_total = ktime.get("allreduce") or 0.0
+    if "dx" in segments and ar_total > segments["dx"]:
+        del segments["dx"]
+        segments["allreduce"] = ar_total
+    return {"ms": phases, "limiting": max(segments, key=segments.get), "allreduce_total_ms": ktime.get("allreduce")}
 
 
 def run_api_drive(mode_args, timeout=600):
