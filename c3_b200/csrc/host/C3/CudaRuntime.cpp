@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <thread>
@@ -130,7 +131,8 @@ class CopyPool {
   bool stop_ = false;
 };
 
-// Pinned staging buffers, each with the event of the last DMA that used it.
+// Pinned staging buffers, each with the event of the last DMA that used it. One set per device:
+// an event can only be recorded on a stream of the device it was created on.
 struct Staging {
   static constexpr size_t kChunk = 8u << 20;
   static constexpr int kBuffers = 3;
@@ -139,9 +141,16 @@ struct Staging {
   cudaEvent_t ev[kBuffers] = {};
   bool ready = false;
 
-  static Staging& instance() {
-    static Staging s;
-    return s;
+  // The set of the current device (the device of the copy's stream and device buffer).
+  static Staging& forCurrentDevice() {
+    static std::mutex mu_all;
+    static std::vector<std::unique_ptr<Staging>> per_device;
+    int dev = 0;
+    checkCuda(cudaGetDevice(&dev), "staging: cudaGetDevice");
+    std::lock_guard<std::mutex> lk(mu_all);
+    if (static_cast<int>(per_device.size()) <= dev) per_device.resize(dev + 1);
+    if (!per_device[dev]) per_device[dev] = std::make_unique<Staging>();
+    return *per_device[dev];
   }
   void init() {  // under mu
     if (ready) return;
@@ -162,7 +171,7 @@ void copyToDevice(void* dst, const void* src, size_t bytes, cudaStream_t stream)
     checkCuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream), "copyToDevice");
     return;
   }
-  Staging& st = Staging::instance();
+  Staging& st = Staging::forCurrentDevice();
   std::lock_guard<std::mutex> lk(st.mu);
   st.init();
   size_t o = 0;
@@ -183,7 +192,7 @@ void copyToHost(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
     checkCuda(cudaStreamSynchronize(stream), "copyToHost: synchronize");
     return;
   }
-  Staging& st = Staging::instance();
+  Staging& st = Staging::forCurrentDevice();
   std::lock_guard<std::mutex> lk(st.mu);
   st.init();
   const size_t n = (bytes + Staging::kChunk - 1) / Staging::kChunk;

@@ -32,8 +32,9 @@ void freeDevice(void* p, cudaStream_t stream);
 // the neighbouring chunk runs, so the link moves pinned-speed transfers although the host
 // tensor itself is not pinned. copyToDevice returns once `src` may be reused (the last DMA may
 // still be in flight on `stream`); copyToHost returns once `dst` holds the data. Small copies
-// (under 4 MiB) are plain cudaMemcpyAsync calls. Large copies from different host threads are
-// serialised on the staging buffers.
+// (under 4 MiB) are plain cudaMemcpyAsync calls. Each device has its own staging buffers (the
+// current device's are used, so `stream` and the device buffer belong to the current device);
+// large copies from different host threads to one device are serialised on them.
 void copyToDevice(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 void copyToHost(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
