@@ -19,6 +19,7 @@
 // variant 1.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -357,7 +358,7 @@ namespace attn {
 
 // 0 = automatic (= 3), 1 = one query tile per CTA, 2 = two query tiles with 128-key blocks,
 // 3 = two query tiles with 64-key blocks and two S buffers per tile.
-static int g_attn_variant = 0;
+static std::atomic<int> g_attn_variant{0};  // process-wide; set by c3cu_set_attn_variant
 
 namespace {
 int encode_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S, uint32_t box_rows = 128) {
@@ -429,7 +430,8 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
   p.causal = causal ? 1 : 0;
   p.O = static_cast<__nv_bfloat16*>(O);
   p.lse = LSE;
-  if (attn::g_attn_variant == 1) {
+  const int variant = attn::g_attn_variant.load(std::memory_order_relaxed);  // one value for the whole call
+  if (variant == 1) {
     static std::atomic<uint64_t> smem_set{0};
     rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd_kernel), attn::SMEM_BYTES,
                               smem_set, "flash_attn_fwd: set shared memory");
@@ -448,7 +450,7 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
-  if (attn::g_attn_variant == 0 || attn::g_attn_variant == 3) {
+  if (variant == 0 || variant == 3) {
     // 64-key blocks: K / V tensor maps with 64-row boxes
     CUtensorMap tk64, tv64;
     if ((rc = attn::encode_bhsd(&tk64, K, B * H, S, 64)) != C3CU_OK) return rc;
@@ -475,6 +477,6 @@ extern "C" int c3cu_set_attn_variant(int variant) {
     c3cu::set_error("set_attn_variant: unknown variant %d", variant);
     return C3CU_ERR_INVALID;
   }
-  c3cu::attn::g_attn_variant = variant;
+  c3cu::attn::g_attn_variant.store(variant, std::memory_order_relaxed);
   return C3CU_OK;
 }
