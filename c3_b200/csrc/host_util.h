@@ -13,7 +13,7 @@
 #include <string>
 #include <utility>
 
-#include "../../include/c3cu.h"
+#include "c3cu.h"
 
 namespace c3cu {
 

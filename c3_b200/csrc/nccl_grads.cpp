@@ -12,7 +12,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/c3cu.h"
+#include "c3cu.h"
 #include "host_util.h"
 
 namespace {
