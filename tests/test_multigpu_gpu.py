@@ -73,8 +73,9 @@ def _worker(rank, world, port, q):
                   flush=True)
             results[f"f32_{trial}"] = float((arb.f32 - ref_f).abs().max() / ref_f.abs().max())
         # split call (c3cu_nvls_allreduce_split): the peer part is an fp32 sum in rank order
-        # rounded once to nearest, so with two ranks (an exact fp32 sum of two bf16 values) it
-        # equals NCCL's fp32 sum rounded to bf16 bit for bit; the switch part as above
+        # rounded once to nearest, so with two ranks (one fp32 addition, the same IEEE result in
+        # either order) it equals NCCL's fp32 sum rounded to bf16 bit for bit; the switch part
+        # as above
         from c3_b200.collective import split_point
         for trial, (frac, pctas, lo, hi, with_f32) in enumerate(
                 [(0.3, 3, 0, nb, True), (0.5, 1, 8 * 1001, nb - 8 * 77, False), (1.0, 7, 0, nb, True),
