@@ -1,5 +1,6 @@
-"""Data-parallel path on 2 GPUs (child processes, one per GPU): the in-switch all-reduce kernel
-against NCCL's all_reduce on the same buffers, the dW GEMM with the all-reduce fused into its
+"""Data-parallel path on 2 GPUs (child processes, one per GPU): the in-switch all-reduce kernels
+(including the split call that sums part of the buffer from peer loads) against NCCL's
+all_reduce on the same buffers, the dW GEMM with the all-reduce fused into its
 epilogue against NCCL's sum of the same partials, the row-sharded training step against the
 one-GPU step on the full batch, and the data-parallel cfg1 MLP step (eager and CUDA-graph
 replay, one NCCL all-reduce of gradients + loss per step) against the one-GPU full-batch step.
