@@ -365,7 +365,13 @@ def default_overlap(world: int) -> tuple[int, int]:
     Measured on B200s (cfg3): 20 CTAs on 20 reserved SMs gave the shortest step with 2 ranks
     (2722 TFLOP/s, against 2370 with no reserve and 16 CTAs) and with 8 ranks (5396 against
     4983). Without a reserve, the all-reduce competes with the CTA-pair dX GEMM's CTAs and
-    runs about twice as long."""
+    runs about twice as long. What the reserve costs dX follows from its tile count: 20 SMs
+    leave 64 of the 74 CTA pairs, and at 2048 and 4096 rows per rank the 128 and 256 output
+    tiles of 256 x 256 take 2 and 4 waves on 64 pairs as on 74, so the reserve is free there;
+    at 8192 rows (2 ranks) the 512 tiles take 8 waves instead of 7, which the shorter
+    all-reduce more than repays. More CTAs (32 on 32 SMs) cost dX a wave at every size and
+    measured slower at 8 ranks; a thread-block cluster per CTA pair changed nothing
+    (c3cu_set_collective_cluster)."""
     return (20, 20) if world > 1 else (16, 0)
 
 
