@@ -16,7 +16,8 @@
 // The default launch is flash_fwd3_kernel (attn3.cuh): two query tiles per CTA sharing each
 // 64-key K / V block, two S buffers per tile, ping-pong softmax warpgroups. flash_fwd2_kernel
 // (attn2.cuh, 128-key blocks, one S buffer per tile) is variant 2 and this single-tile kernel
-// variant 1.
+// variant 1. Variant 4 is flash_fwd3_kernel<true>: the same computation with the two tiles'
+// softmax warps of each SM sub-partition taking turns at their exponentials (experimental).
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -450,17 +451,26 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
     set_error("flash_attn_fwd: grid too large");
     return C3CU_ERR_INVALID;
   }
-  if (variant == 0 || variant == 3) {
+  if (variant == 0 || variant == 3 || variant == 4) {
     // 64-key blocks: K / V tensor maps with 64-row boxes
     CUtensorMap tk64, tv64;
     if ((rc = attn::encode_bhsd(&tk64, K, B * H, S, 64)) != C3CU_OK) return rc;
     if ((rc = attn::encode_bhsd(&tv64, V, B * H, S, 64)) != C3CU_OK) return rc;
+    if (variant == 4) {
+      static std::atomic<uint64_t> smem_set4{0};
+      rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd3_kernel<true>), attn::SMEM_BYTES3,
+                                smem_set4, "flash_attn_fwd: set shared memory");
+      if (rc != C3CU_OK) return rc;
+      attn::flash_fwd3_kernel<true><<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
+                                      static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
+      return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
+    }
     static std::atomic<uint64_t> smem_set3{0};
-    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd3_kernel), attn::SMEM_BYTES3,
+    rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn::flash_fwd3_kernel<false>), attn::SMEM_BYTES3,
                               smem_set3, "flash_attn_fwd: set shared memory");
     if (rc != C3CU_OK) return rc;
-    attn::flash_fwd3_kernel<<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
-                              static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
+    attn::flash_fwd3_kernel<false><<<static_cast<unsigned>(grid), attn::kThreads3, attn::SMEM_BYTES3,
+                                     static_cast<cudaStream_t>(stream)>>>(tq, tk64, tv64, p);
     return cuda_status(cudaGetLastError(), "flash_attn_fwd: launch");
   }
   static std::atomic<uint64_t> smem_set2{0};
@@ -473,7 +483,7 @@ extern "C" int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, 
 }
 
 extern "C" int c3cu_set_attn_variant(int variant) {
-  if (variant < 0 || variant > 3) {
+  if (variant < 0 || variant > 4) {
     c3cu::set_error("set_attn_variant: unknown variant %d", variant);
     return C3CU_ERR_INVALID;
   }

@@ -11,6 +11,14 @@
 //   warp 1      MMA: for j, tile t: O_t += P_{t,j} V_j, then S_{t,j+2} = Q_t K_{j+2}^T into
 //               the buffer P_{t,j} came from (tcgen05.mma ops of one thread run in order)
 //   warps 2..5  softmax of tile 0, warps 6..9 of tile 1 (one thread per row, 64 scores).
+//
+// ALT (variant 4): warps 2+i and 6+i (i = 0..3) share an SM sub-partition and its MUFU unit.
+// Left alone they reach their exponentials at about the same time, so the exponentials of both
+// tiles contend while the TMEM loads, row maxima and P stores of both wait at once. With ALT the
+// two take turns: a warp runs the exponentials of its block only after its partner has finished
+// the partner's previous exponentials (tile 0 goes first), through a token mbarrier per warp
+// (bounded waits; a warp stops waiting once its partner has finished all its blocks, as the
+// causal tiles have different block counts).
 #pragma once
 
 namespace c3cu {
@@ -24,6 +32,25 @@ constexpr int kThreads3 = 320;
 // smem: Q0 | Q1 | (K V) x stages | barriers
 constexpr uint32_t SMEM_BYTES3 = 2 * TILE_BYTES + KV_STAGES3 * 2 * KV_TILE3 + 32 * 8 + 1024;
 
+// Waits for a token mbarrier phase, or until the partner warp has set its done flag (it has no
+// more tokens to hand over). Bounded: records kFaultWaitSoftmax and returns false at the limit.
+__device__ __forceinline__ bool token_wait(uint64_t* bar, uint32_t parity, const volatile int* partner_done) {
+  if (mbar_try_wait(bar, parity) || *partner_done) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity) || *partner_done) return true;
+    if ((++spins & 255u) == 0u) {
+      if (fault_raised()) return false;
+      if (globaltimer_ns() - t0 > C3CU_WAIT_LIMIT_NS) {
+        record_fault(kFaultWaitSoftmax, blockIdx.x & 0xffffu);
+        return false;
+      }
+    }
+  }
+}
+
+template <bool ALT>
 __global__ void __launch_bounds__(kThreads3, 1)
     flash_fwd3_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const Params p) {
@@ -46,6 +73,10 @@ __global__ void __launch_bounds__(kThreads3, 1)
   uint64_t* pv_done = p_full + 2;                // [tile]
   uint64_t* drain = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  // ALT only: token[4 * t + i] is handed to tile t's warp of pair i; done[4 * t + i] is set once
+  // that warp has run its last block (bytes 152..247 of the 256 reserved for barriers)
+  uint64_t* token = drain + 2;
+  int* done = reinterpret_cast<int*>(token + 8);
 
   const uint32_t warp = warp_id_sync();
   const uint32_t lane = lane_id();
@@ -73,6 +104,12 @@ __global__ void __launch_bounds__(kThreads3, 1)
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
+    if constexpr (ALT) {
+      for (int i = 0; i < 8; ++i) {
+        mbar_init(&token[i], 1);
+        done[i] = 0;
+      }
+    }
     fence_mbarrier_init();
     tma_prefetch_desc(&tmq);
     tma_prefetch_desc(&tmk);
@@ -191,6 +228,11 @@ __global__ void __launch_bounds__(kThreads3, 1)
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
+    // ALT: this warp's token and its partner's (the other tile's warp on the same sub-partition)
+    [[maybe_unused]] const uint32_t pair = warp & 3u;
+    [[maybe_unused]] uint64_t* my_token = token + 4 * t + pair;
+    [[maybe_unused]] uint64_t* partner_token = token + 4 * (1 - t) + pair;
+    [[maybe_unused]] const volatile int* partner_done = done + 4 * (1 - t) + pair;
     for (int j = 0; j < n; ++j) {
       const uint32_t s_base = t_base + 64u * (j & 1);
       if (!mbar_wait(&s_full[2 * t + (j & 1)], (j >> 1) & 1u, kFaultWaitAccFull)) { ok = false; break; }
@@ -225,6 +267,15 @@ __global__ void __launch_bounds__(kThreads3, 1)
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
       const float2 nb2 = make_float2(-base, -base);
       float2 rs2 = make_float2(0.f, 0.f);
+      if constexpr (ALT) {
+        // tile 0's exponentials of block j follow tile 1's of block j - 1; tile 1's of block j
+        // follow tile 0's of block j (token phase = number of the partner's finished turns - 1)
+        const bool first = t == 0 && j == 0;
+        if (!first && !token_wait(my_token, static_cast<uint32_t>(t == 0 ? j - 1 : j) & 1u, partner_done)) {
+          ok = false;
+          break;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < BKV3 / 32; ++c) {
         uint32_t w[16];
@@ -237,6 +288,10 @@ __global__ void __launch_bounds__(kThreads3, 1)
           w[i] = pack_bf16x2(e.x, e.y);
         }
         tmem_st_32x32b_x16(s_base + c * 16, w);
+      }
+      if constexpr (ALT) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(partner_token);  // the partner's turn
       }
       l = l * alpha + (rs2.x + rs2.y);
       // Rescaling O needs PV_{t,j-1} complete; unlike the single-buffer kernel, S_{t,j} was
@@ -267,6 +322,11 @@ __global__ void __launch_bounds__(kThreads3, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if constexpr (ALT) {
+      // no more turns from this warp: its partner stops waiting for them
+      __syncwarp();
+      if (lane == 0) *reinterpret_cast<volatile int*>(done + 4 * t + pair) = 1;
     }
     if (ok && n > 0 && mbar_wait(&pv_done[t], (n - 1) & 1u, kFaultWaitAccFull)) {
       tc_fence_after();

@@ -267,7 +267,8 @@ int c3cu_flash_attn_fwd(const void* Q, const void* K, const void* V, void* O, fl
                         c3cu_stream_t stream);
 /* Attention kernel for the calls that follow (process-wide): 0 = default (3); 1 = one
  * 128-row query tile per CTA; 2 = two query tiles per CTA sharing each 128-key K / V block;
- * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM. */
+ * 3 = two query tiles per CTA, 64-key blocks with two S buffers per tile in TMEM; 4 = 3 with
+ * the two tiles' softmax warps taking turns at their exponentials (experimental). */
 int c3cu_set_attn_variant(int variant);
 
 /* ------------------------------------------------------------------ fused dW GEMM + all-reduce

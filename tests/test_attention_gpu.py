@@ -3,6 +3,7 @@ bf16 inputs (no reference implementation exists: parity unpinned). Tolerance: O 
 (normwise and per element with an rms floor; P is rounded to bf16 before P V), LSE within 2e-3
 absolute."""
 import math
+import os
 
 import numpy as np
 import pytest
@@ -83,6 +84,37 @@ def test_flash_attention_kernels_agree(cuda_device, S, causal, variant):
         L.c3cu_set_attn_variant(0)
     assert_bf16_close(O0.float().cpu().numpy(), O1.float().cpu().numpy(), "O two-tile vs one-tile")
     assert (L0 - L1).abs().max().item() <= 1e-3
+
+
+# Variant 4 (the two tiles' exponentials take turns) has not run on a GPU yet; its tests run
+# only when C3_TEST_ATTN_ALT=1.
+_alt = pytest.mark.skipif(os.environ.get("C3_TEST_ATTN_ALT") != "1",
+                          reason="attention variant 4 not yet run on a GPU (C3_TEST_ATTN_ALT=1 runs it)")
+
+
+@_alt
+@pytest.mark.parametrize("S", [64, 192, 384, 1024, 300])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_attention_alternating_exponentials(cuda_device, S, causal):
+    """Variant 4 (variant 3 with the two tiles' exponential phases alternating) against the
+    oracle and bit for bit against variant 3: the turns change only when each warp runs, not
+    what it computes."""
+    from c3_b200 import _lib
+    L = _lib.load()
+    B, H = 2, 3
+    Q, K, V = _qkv(B, H, S, 7 * S + int(causal), cuda_device)
+    try:
+        _lib.check(L.c3cu_set_attn_variant(3), "c3cu_set_attn_variant")
+        O3, L3 = flash_attn_fwd(Q, K, V, causal=causal)
+        _lib.check(L.c3cu_set_attn_variant(4), "c3cu_set_attn_variant")
+        O4, L4 = flash_attn_fwd(Q, K, V, causal=causal)
+        torch.cuda.synchronize()
+    finally:
+        L.c3cu_set_attn_variant(0)
+    from c3_b200 import fault_status
+    fault_status()
+    _check(Q, K, V, O4, L4, causal, [(0, 0), (1, 2)])
+    assert torch.equal(O4, O3) and torch.equal(L4, L3)
 
 
 @pytest.fixture
